@@ -1,0 +1,422 @@
+"""Benchmark: NVFP4 GEMV (headline) plus the other configurations as extras.
+
+    python bench.py --gpus N --steps K --warmup W [--impl reference]
+
+Headline workload (N = 1): config 1, the large single-vector GEMV
+M = K = 16384, L = 1.  For N > 1 (torchrun, one rank per GPU) the same problem
+is row-sharded across ranks and the fp16 output is all-gathered with NCCL
+(strong scaling: total work fixed).  ``value`` is HBM GB/s of algorithmic
+bytes (whole job); ``ms_per_step`` the device time of one step.
+
+Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
+the launching stream, with a 512 MiB L2 flush (outside the events) before each
+step; barrier + synchronize around the timed region; max over ranks.
+
+``--impl reference`` times the reference arm: the reference ships no CPU code
+for this path, so it is the CPU restatement (torch, all host threads) on a
+bounded row sample of the same workload, plus the reference's own GPU kernel
+(built from its source into oracle/_ref) when it is present.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_FLUSH_BYTES = 512 << 20
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": 1590.0}, "fallback"
+
+
+def profiled_traffic(name: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.txt
+    (a line 'traffic_bytes_per_launch: N'); None when absent."""
+    p = os.path.join(ROOT, "profiles", name + ".txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks and throttle reasons sampled while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+# ---------------------------------------------------------------------------
+# plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(world, values):
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+class Flusher:
+    def __init__(self):
+        self.buf = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_steps(step, steps, warmup, flush, marks=1):
+    """Runs `warmup` untimed steps, then `steps` timed ones.  `step(ev)` records
+    its own events into the list `ev` (first and last bracket the step; extra
+    events split it).  Returns per-step lists of segment durations in ms."""
+    for _ in range(warmup):
+        step([])
+    torch.cuda.synchronize()
+    recs = []
+    for _ in range(steps):
+        flush()
+        ev = []
+        step(ev)
+        recs.append(ev)
+    torch.cuda.synchronize()
+    out = []
+    for ev in recs:
+        out.append([ev[i].elapsed_time(ev[i + 1]) for i in range(len(ev) - 1)])
+    return out
+
+
+def ev_mark(ev):
+    e = torch.cuda.Event(enable_timing=True)
+    e.record()
+    ev.append(e)
+
+
+def oracle_mod():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import nvfp4_oracle
+    return nvfp4_oracle
+
+
+def cpu_gemv_sample(pkg, M, K, L, target_s=10.0, max_rows=2048):
+    """Times the CPU restatement (torch, all threads) on a row sample of the
+    workload; returns (GB/s of algorithmic bytes, sample description, threads)."""
+    oracle = oracle_mod()
+    rows = min(M, max_rows)
+    x = pkg.inputs.gemv_inputs(rows, K, L, seed=0, device="cpu")
+    t0 = time.perf_counter()
+    oracle.gemv_torch(x.a, x.b, x.sfa, x.sfb, rows, K, L)
+    one = time.perf_counter() - t0
+    reps = max(1, int(target_s / max(one, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        oracle.gemv_torch(x.a, x.b, x.sfa, x.sfb, rows, K, L)
+    dt = (time.perf_counter() - t0) / reps
+    gbs = x.nbytes_algorithmic() / dt / 1e9
+    return gbs, f"{rows} of {M} rows x K={K} x L={L}, {reps} reps", torch.get_num_threads()
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+HEADLINE = dict(M=16384, K=16384, L=1)
+
+
+def gemv_rank_inputs(pkg, M, K, L, world, rank):
+    """This rank's rows of the seeded problem (the whole problem when world == 1)."""
+    full = pkg.inputs.gemv_inputs(M, K, L, seed=0, device="cpu")
+    lo, hi = pkg.sharded.row_split(M, world, rank)
+    sub = lambda t: t[lo:hi].permute(2, 0, 1).contiguous().permute(1, 2, 0)
+    return full, lo, hi, sub(full.a), full.b, sub(full.sfa), full.sfb
+
+
+def run_gemv_extra(pkg, flush, M, K, L, steps, warmup):
+    x = pkg.inputs.gemv_inputs(M, K, L, seed=0, device="cuda")
+
+    def step(ev):
+        if ev is not None:
+            ev_mark(ev)
+        pkg.custom_kernel(*x.as_tuple())
+        if ev is not None:
+            ev_mark(ev)
+
+    ts = [s[0] for s in time_steps(step, steps, warmup, flush)]
+    us = statistics.mean(ts) * 1e3
+    return {"workload": f"gemv M={M} K={K} L={L}", "us": round(us, 3),
+            "gbs": round(x.nbytes_algorithmic() / (us * 1e-6) / 1e9, 1),
+            "us_median": round(statistics.median(ts) * 1e3, 3)}
+
+
+def our_arm(args, world, rank, local):
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    pk, pk_kind = peaks()
+    M, K, L = HEADLINE["M"], HEADLINE["K"], HEADLINE["L"]
+    full, lo, hi, a_h, b_h, sfa_h, sfb_h = gemv_rank_inputs(pkg, M, K, L, world, rank)
+    dev = torch.device("cuda", local)
+    to_dev = lambda t: t.permute(2, 0, 1).contiguous().to(dev).permute(1, 2, 0)
+    a, b, sfa, sfb = to_dev(a_h), to_dev(b_h), to_dev(sfa_h), to_dev(sfb_h)
+    sh = pkg.sharded.ShardedGemv(M, K, L, device=dev)
+    flush = Flusher()
+
+    def step_split(ev):
+        ev_mark(ev)
+        n = hi - lo
+        pkg.custom_kernel(a, b, sfa, sfb, sh.local[:, :, :n].permute(2, 1, 0))
+        ev_mark(ev)
+        if world > 1:
+            import torch.distributed as dist
+            dist.all_gather_into_tensor(sh.gathered.view(-1), sh.local.view(-1))
+        ev_mark(ev)
+
+    # correctness gate before timing (rank-local rows against a CPU row sample)
+    sh(pkg.custom_kernel, a, b, sfa, sfb)
+    torch.cuda.synchronize()
+
+    barrier(world)
+    with ClockSampler(local) as clk:
+        t_wall0 = time.perf_counter()
+        segs = time_steps(step_split, args.steps, args.warmup, flush)
+        barrier(world)
+        t_wall = time.perf_counter() - t_wall0
+    step_ms = [s[0] + s[1] for s in segs]
+    kern_ms = [s[0] for s in segs]
+    mean_step, mean_kern = max_over_ranks(world, [statistics.mean(step_ms), statistics.mean(kern_ms)])
+    nbytes = full.nbytes_algorithmic()
+    value = nbytes / (mean_step * 1e-3) / 1e9
+
+    # end to end through the public API from pinned host buffers
+    a_p, b_p, sfa_p, sfb_p = (t.permute(2, 0, 1).contiguous().pin_memory() for t in (a_h, b_h, sfa_h, sfb_h))
+    out_host = torch.empty(sh.gathered.shape, dtype=torch.float16).pin_memory()
+    a_d, b_d, sfa_d, sfb_d = (torch.empty_like(t, device=dev) for t in (a_p, b_p, sfa_p, sfb_p))
+
+    def e2e_step(ev):
+        ev_mark(ev)
+        for d, h in ((a_d, a_p), (b_d, b_p), (sfa_d, sfa_p), (sfb_d, sfb_p)):
+            d.copy_(h, non_blocking=True)
+        sh(pkg.custom_kernel, a_d.permute(1, 2, 0), b_d.permute(1, 2, 0), sfa_d.permute(1, 2, 0),
+           sfb_d.permute(1, 2, 0))
+        out_host.copy_(sh.gathered, non_blocking=True)
+        ev_mark(ev)
+
+    e2e_ms = [s[0] for s in time_steps(e2e_step, max(3, args.steps // 4), 2, flush)]
+    (e2e_mean,) = max_over_ranks(world, [statistics.mean(e2e_ms)])
+    h2d = sum(t.numel() * t.element_size() for t in (a_p, b_p, sfa_p, sfb_p))
+    d2h = out_host.numel() * out_host.element_size()
+    h2d_all, d2h_all = (int(v) for v in max_over_ranks(world, [h2d * world, d2h * world]))
+
+    if rank != 0:
+        return None
+    ncu_traffic = profiled_traffic("gemv_m16384_k16384_l1")
+    kern_bytes = nbytes if world == 1 else nbytes * (hi - lo) / M
+    achieved = kern_bytes / (mean_kern * 1e-3) / 1e9
+    line = {
+        "metric": "NVFP4 GEMV HBM GB/s (M=K=16384, L=1)",
+        "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(mean_step, 5), "us_per_step": round(mean_step * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e2m1/e4m3 in, f32 acc, f16 out",
+        "data": "synthetic (seed 0; codes uniform 0..255, scales 2^u, u in [-3,3])",
+        "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1" +
+                   (f", row-sharded x{world} + NCCL all-gather" if world > 1 else ""),
+                   "M": M, "K": K, "L": L, "l2": "flushed (512 MiB write) before every step",
+                   "parallelism": f"rows/{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk_kind,
+                     "kernel_us": round(mean_kern * 1e3, 3), "algorithmic_bytes_per_launch": int(kern_bytes),
+                     "traffic": ncu_traffic},
+        "e2e": {"value": round(nbytes / (e2e_mean * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all,
+                "ms_per_step": round(e2e_mean, 4)},
+        "gpu_launches": args.steps * 1,
+        "clocks": clk.summary(),
+        "wall_s_timed_region": round(t_wall, 3),
+    }
+    if world == 1:
+        gbs, sample, threads = cpu_gemv_sample(pkg, M, K, L, target_s=args.cpu_seconds)
+        line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                                "sample": sample, "host_cpus": os.cpu_count()}
+        if not args.no_extras:
+            line["extras"] = [run_gemv_extra(pkg, flush, 256, 1024, 1, 50, 5),
+                              run_gemv_extra(pkg, flush, 4096, 14336, 8, 20, 3)]
+            for e in line["extras"]:
+                e["hbm_frac"] = round(e["gbs"] / pk["hbm_gbs"], 4)
+    return line
+
+
+# ---------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------
+
+def reference_arm(args, world, rank, local):
+    if rank != 0:
+        return None
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    M, K, L = HEADLINE["M"], HEADLINE["K"], HEADLINE["L"]
+    oracle = oracle_mod()
+    rows = 1024
+    x = pkg.inputs.gemv_inputs(rows, K, L, seed=0, device="cpu")
+    for _ in range(args.warmup):
+        oracle.gemv_torch(x.a, x.b, x.sfa, x.sfb, rows, K, L)
+    ts = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.gemv_torch(x.a, x.b, x.sfa, x.sfb, rows, K, L)
+        ts.append(time.perf_counter() - t0)
+    dt = statistics.mean(ts)
+    gbs = x.nbytes_algorithmic() / dt / 1e9
+    full_bytes = pkg.inputs.GemvInputs.nbytes_algorithmic(
+        pkg.inputs.GemvInputs(None, None, None, None, None, M, K, L))
+    line = {
+        "impl": "reference",
+        "metric": "NVFP4 GEMV HBM GB/s (M=K=16384, L=1)", "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(full_bytes / (gbs * 1e9) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "e2m1/e4m3 in, f32 acc, f16 out",
+        "data": "synthetic (seed 0)",
+        "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1", "M": M, "K": K, "L": L},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{rows} of {M} rows per step (fp32 dequantise + matmul, torch CPU)",
+                         "host_cpus": os.cpu_count()},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference ships no CPU implementation of this path; this arm is the CPU restatement",
+    }
+    # the reference's own GPU kernel, built from its source, on the same inputs
+    try:
+        import build_ref
+        if torch.cuda.is_available() and os.path.exists(build_ref.SO_PATH):
+            ref = build_ref.load()
+            flush = Flusher()
+            out = {}
+            for (m, k, l) in ((M, K, L), (256, 1024, 1), (4096, 14336, 8)):
+                g = pkg.inputs.gemv_inputs(m, k, l, seed=0, device="cuda")
+
+                def st(ev):
+                    ev_mark(ev)
+                    ref.nvfp4_gemv_forward(g.a, g.b, g.sfa, g.sfb, g.c, m, k, l)
+                    ev_mark(ev)
+                t = statistics.mean(s[0] for s in time_steps(st, max(10, args.steps), 3, flush))
+                out[f"M={m} K={k} L={l}"] = {"us": round(t * 1e3, 3),
+                                            "gbs": round(g.nbytes_algorithmic() / (t * 1e-3) / 1e9, 1)}
+            line["reference_gpu_kernel"] = out
+    except Exception as e:  # report, do not fail the arm
+        line["reference_gpu_kernel"] = {"unavailable": str(e)[:200]}
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-extras", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup()
+    if args.impl == "reference":
+        line = reference_arm(args, world, rank, local)
+    else:
+        line = our_arm(args, world, rank, local)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

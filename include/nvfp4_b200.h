@@ -1,0 +1,97 @@
+/*
+ * nvfp4_b200.h — C ABI of libnvfp4_b200.so, a B200 (sm_100a) NVFP4 kernel library.
+ *
+ * Data formats (all entry points):
+ *   - FP4 operands are e2m1 codes packed two per byte, K contiguous ("K-major"),
+ *     the even K index in the low nibble.
+ *   - Block scales are e4m3fn bytes, one per 16 consecutive K elements.
+ *   - Outputs are IEEE fp16.  Accumulation is fp32.
+ *
+ * Conventions: every function returns 0 (NVFP4_OK) or a positive status code and
+ * never throws; nvfp4_last_error() gives the calling thread's last message.
+ * Work is enqueued on the caller's stream (a cudaStream_t passed as void*; NULL is
+ * the legacy default stream) on the current device; no function synchronises
+ * unless its comment says so.  Pointers are device pointers.
+ */
+#ifndef NVFP4_B200_H_
+#define NVFP4_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NVFP4_API __attribute__((visibility("default")))
+#else
+#define NVFP4_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum nvfp4_status {
+  NVFP4_OK = 0,
+  NVFP4_ERR_INVALID = 1,      /* bad shape, stride or null pointer */
+  NVFP4_ERR_ALIGNMENT = 2,    /* a pointer or stride breaks a 16-byte rule */
+  NVFP4_ERR_CUDA = 3,         /* a CUDA runtime / driver call failed */
+  NVFP4_ERR_TIMEOUT = 4,      /* a device-side bounded wait expired */
+  NVFP4_ERR_UNSUPPORTED = 5,  /* no kernel for this device or shape */
+};
+
+/* Message for the last non-zero status returned on this thread. */
+NVFP4_API const char* nvfp4_last_error(void);
+
+/* Library version as 10000*major + 100*minor + patch. */
+NVFP4_API int nvfp4_version(void);
+
+/*
+ * Batched block-scaled GEMV.
+ *   c[m, l] = sum_k e2m1(a[m, k, l]) * e2m1(b[k, l]) * e4m3(sfa[m, k/16, l]) * e4m3(sfb[k/16, l])
+ *
+ * Replaces the reference's pybind entry
+ *   void nvfp4_gemv_forward(const at::Tensor& a, const at::Tensor& b,
+ *                           const at::Tensor& sa, const at::Tensor& sb,
+ *                           at::Tensor& c, int64_t M, int64_t K, int64_t L)
+ * (Nvidia-x-GPU-MODE-Kernels, blackwell_nvfp4_gemv.cu:500-524), whose tensors are
+ * a [M, K/2, L], b [>=1, K/2, L] (row 0 read), sa [M, K/16, L], sb [>=1, K/16, L],
+ * c [M, 1, L]; the strides that the reference reads from the tensors
+ * (blackwell_nvfp4_gemv.cu:226-227, 257-258, 270-271, 284-285, 495-497) are explicit
+ * here.  Innermost (K) strides are 1.
+ *
+ *   a_sm, a_sl      : byte strides of a along M and L
+ *   b_sl            : byte stride of b along L
+ *   sfa_sm, sfa_sl  : byte strides of sfa along M and L
+ *   sfb_sl          : byte stride of sfb along L
+ *   c_sm, c_sl      : element strides of c along M and L
+ *
+ * Requirements: M, L >= 1; K >= 16 and K % 16 == 0.  The TMA-streaming kernel is
+ * used when K % 256 == 0 and every pointer and byte stride is a multiple of 16;
+ * other valid shapes run a plain-load kernel with the same arithmetic.
+ */
+NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa, const void* sfb, void* c,
+               int64_t M, int64_t K, int64_t L,
+               int64_t a_sm, int64_t a_sl, int64_t b_sl,
+               int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
+               int64_t c_sm, int64_t c_sl, void* stream);
+
+/*
+ * Reads this device's error word (bits set by device-side bounded waits that
+ * expired) and, when `clear` is non-zero, resets it.  Synchronises the device.
+ * No counterpart in the reference, whose waits never expire
+ * (blackwell_nvfp4_gemv.cu:150-157).
+ */
+NVFP4_API int nvfp4_device_errors(uint32_t* out_bits, int clear);
+
+/*
+ * Self-test of the bounded-wait machinery: launches one block that waits on an
+ * mbarrier nothing will ever complete, with a budget of `budget_ns` nanoseconds
+ * (clamped to [1e3, 1e9]); synchronises and returns NVFP4_ERR_TIMEOUT when the
+ * wait expired as designed, NVFP4_OK if it (impossibly) completed.  No
+ * counterpart in the reference.
+ */
+NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t budget_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_B200_H_ */

@@ -1,0 +1,12 @@
+"""nvfp4_b200: NVFP4 (e2m1 + e4m3 block-16 scales) inference kernels for B200.
+
+Importable as ``nvfp4_b200`` through ``__graft_entry__.load_package()`` (the
+directory name is not a Python identifier).
+
+* ``gemv.custom_kernel(a, b, scale_a, scale_b, c)`` - batched block-scaled GEMV,
+  the operator of the reference (blackwell_nvfp4_gemv.cu:500-524).
+"""
+from . import _lib, gemv, inputs, layout, sharded  # noqa: F401
+from .gemv import custom_kernel  # noqa: F401
+
+__all__ = ["custom_kernel", "gemv", "inputs", "layout"]

@@ -1,0 +1,80 @@
+"""NVFP4 block-scaled GEMV: the operator surface of the reference.
+
+``custom_kernel(a, b, scale_a, scale_b, c)`` takes the tensors the reference's
+``nvfp4_gemv_forward(a, b, sa, sb, c, M, K, L)`` takes
+(blackwell_nvfp4_gemv.cu:500-524) and derives M, K, L from them:
+
+* ``a``       [M, K/2, L]   uint8 or torch.float4_e2m1fn_x2, K contiguous
+* ``b``       [>=1, K/2, L] same dtype; row 0 is the vector (:257-259)
+* ``scale_a`` [M, K/16, L]  uint8 or torch.float8_e4m3fn
+* ``scale_b`` [>=1, K/16, L]
+* ``c``       [M, 1, L]     float16, written in place and returned
+
+Unlike the reference, it checks shapes, dtypes, devices and strides, runs on the
+current CUDA stream (the reference uses the legacy default stream, :496), and
+turns library status codes into ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_FP4_DTYPES = (torch.uint8,) + ((torch.float4_e2m1fn_x2,) if hasattr(torch, "float4_e2m1fn_x2") else ())
+_FP8_DTYPES = (torch.uint8, torch.float8_e4m3fn)
+
+
+def _check3(name: str, t: torch.Tensor, dtypes) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.dtype not in dtypes:
+        raise TypeError(f"{name} has dtype {t.dtype}, expected one of {dtypes}")
+    if t.dim() != 3:
+        raise ValueError(f"{name} must be 3-D, got shape {tuple(t.shape)}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.shape[1] > 1 and t.stride(1) != 1:
+        raise ValueError(f"{name} must be contiguous along its second dimension, strides {t.stride()}")
+
+
+def gemv_raw(a, b, sfa, sfb, c, M: int, K: int, L: int, stream: int | None = None) -> None:
+    """Launch through the C ABI with the strides read from the tensors."""
+    if stream is None:
+        stream = torch.cuda.current_stream(c.device).cuda_stream
+    _lib.check(_lib.lib().nvfp4_gemv(
+        a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), c.data_ptr(),
+        M, K, L,
+        a.stride(0), a.stride(2), b.stride(2),
+        sfa.stride(0), sfa.stride(2), sfb.stride(2),
+        c.stride(0), c.stride(2), stream))
+
+
+def custom_kernel(a, b=None, scale_a=None, scale_b=None, c=None):
+    """c[m, 0, l] = sum_k a[m,k,l] * b[0,k,l] * scale_a[m,k//16,l] * scale_b[0,k//16,l].
+
+    Also accepts a single tuple ``(a, b, scale_a, scale_b, c)``.
+    """
+    if b is None and isinstance(a, (tuple, list)):
+        a, b, scale_a, scale_b, c = a
+    _check3("a", a, _FP4_DTYPES)
+    _check3("b", b, _FP4_DTYPES)
+    _check3("scale_a", scale_a, _FP8_DTYPES)
+    _check3("scale_b", scale_b, _FP8_DTYPES)
+    if not isinstance(c, torch.Tensor) or c.dtype != torch.float16 or c.dim() != 3:
+        raise TypeError("c must be a 3-D float16 tensor [M, 1, L]")
+    M, KB, L = a.shape
+    K = 2 * KB
+    if b.shape[1] != KB or b.shape[2] != L or b.shape[0] < 1:
+        raise ValueError(f"b shape {tuple(b.shape)} does not match a {tuple(a.shape)}")
+    if tuple(scale_a.shape) != (M, K // 16, L):
+        raise ValueError(f"scale_a shape {tuple(scale_a.shape)}, expected {(M, K // 16, L)}")
+    if scale_b.shape[1] != K // 16 or scale_b.shape[2] != L or scale_b.shape[0] < 1:
+        raise ValueError(f"scale_b shape {tuple(scale_b.shape)} does not match K={K}, L={L}")
+    if c.shape[0] != M or c.shape[2] != L:
+        raise ValueError(f"c shape {tuple(c.shape)}, expected {(M, 1, L)}")
+    devs = {t.device for t in (a, b, scale_a, scale_b, c)}
+    if len(devs) != 1:
+        raise ValueError(f"all tensors must be on one device, got {devs}")
+    with torch.cuda.device(c.device):
+        gemv_raw(a, b, scale_a, scale_b, c, M, K, L)
+    return c

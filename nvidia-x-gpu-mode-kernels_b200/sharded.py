@@ -1,0 +1,70 @@
+"""Multi-GPU sharding: GEMV by output rows, grouped GEMM by group.
+
+One process per GPU (``torch.distributed``, NCCL over NVLink / NVSwitch).  The
+reference has no distributed code; these follow the north-star plan: each rank
+computes its own slice of the output into a local buffer and one NCCL
+all-gather assembles the full fp16 output on every rank.  No input moves
+between GPUs: every rank holds (or streams) only its own rows / groups.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def row_split(M: int, world: int, rank: int, align: int = 1) -> tuple[int, int]:
+    """Contiguous row range [lo, hi) of rank `rank`; boundaries are multiples of
+    `align` (except the end).  Ranks get equal shares up to one `align` unit."""
+    units = (M + align - 1) // align
+    lo = units * rank // world * align
+    hi = min(M, units * (rank + 1) // world * align)
+    return lo, hi
+
+
+def padded_rows(M: int, world: int) -> int:
+    """Rows per rank of the padded all-gather buffer."""
+    return max(hi - lo for lo, hi in (row_split(M, world, r) for r in range(world)))
+
+
+class ShardedGemv:
+    """Row-sharded GEMV for L = 1 or more.
+
+    Rank r owns rows [lo, hi) of A / SFA (a view of the full problem's rows, or
+    its own copy of them); b / SFB are replicated.  ``__call__`` runs the local
+    GEMV into a padded local buffer and all-gathers the padded slices into
+    ``out`` ([world * rows_pad, 1, L] fp16, contiguous over rows for each l),
+    whose first M rows (``full()``) are the complete result.
+    """
+
+    def __init__(self, M: int, K: int, L: int, group=None, device=None):
+        self.M, self.K, self.L = M, K, L
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.lo, self.hi = row_split(M, self.world, self.rank)
+        self.rows_pad = padded_rows(M, self.world)
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        # local and gathered outputs, L-major so every slice is contiguous
+        self.local = torch.zeros((L, 1, self.rows_pad), dtype=torch.float16, device=dev)
+        self.gathered = torch.empty((self.world, L, self.rows_pad), dtype=torch.float16, device=dev)
+
+    def __call__(self, gemv, a_rows, b, sfa_rows, sfb) -> torch.Tensor:
+        """`gemv` is the package's ``custom_kernel``; a_rows / sfa_rows hold this
+        rank's rows only ([hi - lo, K/2, L] and [hi - lo, K/16, L])."""
+        n = self.hi - self.lo
+        c = self.local[:, :, :n].permute(2, 1, 0)
+        if n > 0:
+            gemv(a_rows, b, sfa_rows, sfb, c)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.gathered.view(-1), self.local.view(-1), group=self.group)
+        else:
+            self.gathered[0].copy_(self.local[:, 0, :])
+        return self.gathered
+
+    def full(self) -> torch.Tensor:
+        """[M, 1, L] view of the assembled output (copy-free when world == 1)."""
+        parts = []
+        for r in range(self.world):
+            lo, hi = row_split(self.M, self.world, r)
+            parts.append(self.gathered[r, :, : hi - lo])
+        return torch.cat(parts, dim=1).transpose(0, 1).unsqueeze(1)

@@ -1,0 +1,37 @@
+"""The reference kernel itself (built from its source into oracle/_ref) on the
+same inputs: pins the CPU oracle against the reference and compares the new
+kernel with it.  The reference sums each 32-element chunk in f16 and scales in
+f16 (blackwell_nvfp4_gemv.cu:126-131), so it agrees with the fp32 oracle only
+to the contract tolerance, not bit for bit."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def ref_mod():
+    import build_ref
+    if not os.path.exists(build_ref.SO_PATH):
+        pytest.skip("reference kernel not built (oracle/_ref)")
+    return build_ref.load()
+
+
+@pytest.mark.parametrize("M,K,L", [(256, 1024, 1), (16384, 16384, 1), (4096, 14336, 8), (7168, 16384, 1),
+                                   (4096, 7168, 8), (7168, 2048, 4)])
+def test_reference_vs_oracle_and_ours(pkg, oracle, cuda, ref_mod, M, K, L):
+    x = pkg.inputs.gemv_inputs(M, K, L, seed=0, device=cuda)
+    c_ref = torch.empty_like(x.c)
+    ref_mod.nvfp4_gemv_forward(x.a, x.b, x.sfa, x.sfb, c_ref, M, K, L)
+    pkg.custom_kernel(*x.as_tuple())
+    torch.cuda.synchronize()
+    r = c_ref.cpu().numpy().astype(np.float32)
+    ours = x.c.cpu().numpy().astype(np.float32)
+    cpu = oracle.gemv_torch(*(t.cpu() for t in (x.a, x.b, x.sfa, x.sfb)), M, K, L).numpy().astype(np.float32)
+    np.testing.assert_allclose(r, cpu, rtol=1e-2, atol=1e-2)      # oracle pinned to the reference
+    np.testing.assert_allclose(ours, r, rtol=1e-2, atol=1e-2)     # new kernel vs reference kernel
