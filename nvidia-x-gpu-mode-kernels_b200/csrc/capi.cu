@@ -4,6 +4,7 @@
 #include <mutex>
 #include "ptx.cuh"
 #include "common.h"
+#include "tmap.h"
 
 namespace nvfp4 {
 
@@ -63,6 +64,44 @@ int sm_count() {
     g_sms[dev] = n;
   }
   return g_sms[dev];
+}
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  if (g_encode) return g_encode;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  return g_encode;
+}
+}  // namespace
+
+int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo) {
+  auto fn = encode_fn();
+  if (!fn) return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bd[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bd[i] = box[i];
+    es[i] = 1;
+    if (i + 1 < rank) gs[i] = strides_bytes[i];
+  }
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), gd, gs, bd, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): rank %d dims[0]=%llu box[0]=%u", (int)r,
+                rank, (unsigned long long)dims[0], box[0]);
+  return NVFP4_OK;
 }
 
 }  // namespace nvfp4

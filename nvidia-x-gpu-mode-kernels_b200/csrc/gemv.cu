@@ -2,33 +2,42 @@
 //
 //   c[m, l] = sum_k e2m1(A[m,k,l]) e2m1(b[k,l]) e4m3(SFA[m,k/16,l]) e4m3(SFB[k/16,l])
 //
-// The reference (blackwell_nvfp4_gemv.cu:295-475) streams one tensor-map tile
-// per K step into a single shared buffer and computes with all threads, so loads
-// and math alternate inside each CTA.  This kernel is HBM-streaming instead:
+// The reference (blackwell_nvfp4_gemv.cu:295-475) loads one tile per K step
+// into a single shared buffer and computes with all threads, so loads and math
+// alternate inside each CTA.  This kernel streams HBM instead:
 //
-//   * a persistent grid (a multiple of the SM count) splits the M*L output rows
-//     into equal contiguous ranges, one per CTA, so every CTA streams the same
-//     number of bytes;
-//   * one producer warp fills a STAGES-deep shared-memory ring with 1-D bulk
-//     (TMA) copies: each lane copies one row's K-slice of A and of SFA, and the
-//     matching slice of b/SFB rides along in the same stage;
-//   * CONSUMER_WARPS warps own rows; each lane owns 16-byte chunks (32 e2m1 codes,
-//     two scale blocks).  b is decoded to f16x2 once per stage per warp and kept
-//     in registers while the warp walks its rows;
-//   * e2m1 -> f16x2 with cvt.rn.f16x2.e2m1x2, products summed with fma.rn.f16x2
-//     inside a 16-element block.  Each half-lane sums 8 products that are
-//     multiples of 1/4 below 36 in magnitude, so every partial sum is a multiple
-//     of 1/4 below 512 and f16 holds it exactly.  The block sum is widened to
-//     f32 and scaled by sfa*sfb in f32 (exact: 4 x 4 significant bits), then
-//     accumulated in f32 - unlike the reference, which scales and sums in f16
-//     (:126-131) and overflows for scale products above 65504;
-//   * the lanes' partial sums of a row meet in a xor-shuffle reduction and one
-//     lane stores the fp16 result.
+//   * work unit = a tile of ROWS output rows of one batch l.  The tiles are
+//     split into equal contiguous ranges, one per CTA of a persistent grid
+//     (SM count x MINB CTAs), so every CTA streams the same number of bytes;
+//   * one producer thread fills a STAGES-deep shared-memory ring: per stage one
+//     tensor-map TMA box of A (ROWS rows x KTB bytes, read as u64 elements so a
+//     row slice of up to 2 KB is one box row), one box of SFA (ROWS x KTB/8),
+//     and the matching slices of b and SFB.  Whole-tile boxes keep the TMA
+//     issue count at four per stage (per-row 1-D bulk copies measured at under
+//     5 TB/s even with the math switched off).  Rows past M and K past the end
+//     read as zeros (TMA out-of-bounds fill) and contribute nothing;
+//   * CW consumer warps split a stage by K: warp w takes 512-byte column chunk
+//     w % NCH of every row in its row group w / NCH, so it decodes its slice of
+//     b once per stage (to f16x2 registers) and reuses it for RPW rows;
+//   * per lane, 16 bytes = 32 e2m1 codes = two scale blocks.  Codes go to f16x2
+//     with cvt.rn.f16x2.e2m1x2 and multiply-add into f16x2 accumulators inside
+//     a 16-element block.  A half-lane sums at most 8 products, each a multiple
+//     of 1/4 below 36 in magnitude, so every partial sum is a multiple of 1/4
+//     below 512 and f16 represents it exactly.  The block sum is widened to f32
+//     and scaled by sfa*sfb in f32 (exact: 4 x 4 significant bits), then
+//     accumulated in f32.  The reference instead scales and sums in f16
+//     (:126-131), which rounds, and overflows once sfa*sfb exceeds 65504;
+//   * at the end of a tile each warp reduces its per-row partials across lanes
+//     (xor shuffles), the NCH column chunks of a row meet in shared memory, and
+//     one thread per row stores the fp16 result.
 //
 // Every wait is bounded (2 s) and reports into the device error word.
 #include <cuda_fp16.h>
+#include <cstring>
+#include <mutex>
 #include "ptx.cuh"
 #include "common.h"
+#include "tmap.h"
 
 namespace nvfp4 {
 namespace {
@@ -46,40 +55,89 @@ struct GemvArgs {
   uint32_t* err;
 };
 
-template <int ROWS_, int KTB_, int STAGES_, int CONSUMER_WARPS_>
-struct GemvCfg {
-  static constexpr int ROWS = ROWS_;            // rows per stage tile
-  static constexpr int KTB = KTB_;              // A bytes per row per stage
-  static constexpr int STAGES = STAGES_;
-  static constexpr int CW = CONSUMER_WARPS_;
-  static constexpr int THREADS = (CW + 1) * 32;
-  static constexpr int SFB_BYTES = KTB / 8;     // scale bytes per row per stage
-  static constexpr int NCH = KTB / 512;         // 16-byte chunks per lane per row
-  static constexpr int RPW = (ROWS + CW - 1) / CW;  // rows per warp per tile (max)
-  static constexpr int OFF_SFA = ROWS * KTB;
-  static constexpr int OFF_B = OFF_SFA + ROWS * SFB_BYTES;
-  static constexpr int OFF_SFB = OFF_B + KTB;
-  static constexpr int STAGE_BYTES = ((OFF_SFB + SFB_BYTES) + 127) / 128 * 128;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 2 * STAGES * 8 + 16;
-  static_assert(KTB % 512 == 0, "KTB must cover whole warp-wide chunk rows");
-  static_assert(ROWS <= 32, "one producer lane per row");
+struct GemvMaps {
+  CUtensorMap a, sfa, b, sfb;
 };
 
-// The rows a CTA owns: [row_begin, row_end) of the flattened (l, m) space.
-__device__ __forceinline__ void cta_rows(int64_t total, int64_t& r0, int64_t& r1) {
-  const int64_t g = gridDim.x, c = blockIdx.x;
-  r0 = total * c / g;
-  r1 = total * (c + 1) / g;
+// ROWS rows x KTB A-bytes per stage; CW consumer warps; MINB CTAs per SM.
+// MODE 0 computes; MODE 1 only streams (consumers release stages untouched) and
+// exists to measure the copy pipeline's ceiling during tuning.
+template <int ROWS_, int KTB_, int STAGES_, int CW_, int MINB_ = 1, int MODE_ = 0>
+struct GemvCfg {
+  static constexpr int ROWS = ROWS_;
+  static constexpr int KTB = KTB_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int CW = CW_;
+  static constexpr int MINB = MINB_;
+  static constexpr int MODE = MODE_;
+  static constexpr int THREADS = (CW + 1) * 32;
+  static constexpr int NCH = KTB / 512;          // 512-byte column chunks per row
+  static constexpr int GROUPS = CW / NCH;        // row groups
+  static constexpr int RPW = ROWS / GROUPS;      // rows per consumer warp
+  static constexpr int SFK = KTB / 8;            // scale bytes per row per stage
+  static constexpr int OFF_SFA = ROWS * KTB;
+  static constexpr int OFF_B = ((OFF_SFA + ROWS * SFK) + 127) / 128 * 128;
+  static constexpr int OFF_SFB = OFF_B + KTB;
+  static constexpr int STAGE_BYTES = ((OFF_SFB + SFK) + 127) / 128 * 128;
+  static constexpr uint32_t TX = ROWS * KTB + ROWS * SFK + KTB + SFK;
+  static constexpr int OFF_RED = STAGES * STAGE_BYTES;                  // float [2][ROWS][NCH]
+  static constexpr int OFF_BAR = OFF_RED + 2 * ROWS * NCH * 4;
+  static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 128;           // + alignment slack
+  static_assert(KTB % 512 == 0 && KTB <= 2048, "KTB: 512-byte chunks, box row <= 256 u64");
+  static_assert(CW % NCH == 0 && ROWS % GROUPS == 0, "warps must tile (rows x chunks)");
+  static_assert(ROWS <= 256, "TMA box height");
+};
+
+}  // namespace
+
+namespace {
+
+// One 16-byte chunk (two 16-element scale blocks) of a row against the
+// decoded b chunk: returns the f32 contribution sum_blk blocksum * sfa * sfb.
+__device__ __forceinline__ float chunk_dot(const uint4 av, uint32_t sfa2, const uint32_t (&bh)[16],
+                                           float sb0, float sb1) {
+  uint32_t h[4], p0, p1, q0, q1;
+  cvt_e2m1x8(av.x, h);
+  p0 = hfma2(h[0], bh[0], 0u);
+  p1 = hfma2(h[1], bh[1], 0u);
+  p0 = hfma2(h[2], bh[2], p0);
+  p1 = hfma2(h[3], bh[3], p1);
+  cvt_e2m1x8(av.y, h);
+  p0 = hfma2(h[0], bh[4], p0);
+  p1 = hfma2(h[1], bh[5], p1);
+  p0 = hfma2(h[2], bh[6], p0);
+  p1 = hfma2(h[3], bh[7], p1);
+  cvt_e2m1x8(av.z, h);
+  q0 = hfma2(h[0], bh[8], 0u);
+  q1 = hfma2(h[1], bh[9], 0u);
+  q0 = hfma2(h[2], bh[10], q0);
+  q1 = hfma2(h[3], bh[11], q1);
+  cvt_e2m1x8(av.w, h);
+  q0 = hfma2(h[0], bh[12], q0);
+  q1 = hfma2(h[1], bh[13], q1);
+  q0 = hfma2(h[2], bh[14], q0);
+  q1 = hfma2(h[3], bh[15], q1);
+  // each half-lane of p0+p1 sums 8 products: exact in f16 (see file comment)
+  const uint32_t p = hadd2(p0, p1), q = hadd2(q0, q1);
+  float sa0, sa1, x0, y0, x1, y1;
+  h2_to_f2(cvt_e4m3x2(sfa2), sa0, sa1);
+  h2_to_f2(p, x0, y0);
+  h2_to_f2(q, x1, y1);
+  return fmaf(x0 + y0, sa0 * sb0, (x1 + y1) * (sa1 * sb1));
 }
 
 template <class C>
-__global__ void __launch_bounds__(C::THREADS, 1) gemv_tma_kernel(const __grid_constant__ GemvArgs p) {
-  extern __shared__ __align__(128) uint8_t smem[];
+__global__ void __launch_bounds__(C::THREADS, C::MINB)
+gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ GemvArgs p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 127u) & ~127u;
+  uint8_t* smem = smem_raw + (sbase - raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar_full = sbase + C::STAGES * C::STAGE_BYTES;
+  const uint32_t bar_full = sbase + C::OFF_BAR;
   const uint32_t bar_empty = bar_full + 8 * C::STAGES;
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -90,136 +148,106 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemv_tma_kernel(const __grid_co
   }
   __syncthreads();
 
-  const int64_t M = p.M, KB = p.K / 2;  // KB: A bytes per row
-  const int nk = (int)((KB + C::KTB - 1) / C::KTB);
-  int64_t r0, r1;
-  cta_rows(M * p.L, r0, r1);
+  const int64_t M = p.M;
+  const int nk = (int)((p.K / 2 + C::KTB - 1) / C::KTB);
+  const int64_t tpl = (M + C::ROWS - 1) / C::ROWS;  // tiles per batch
+  const int64_t ntiles = tpl * p.L;
+  const int64_t t0 = ntiles * blockIdx.x / gridDim.x, t1 = ntiles * (blockIdx.x + 1) / gridDim.x;
 
   if (warp == C::CW) {
-    // ---------------- producer warp ----------------
-    const uint64_t pol_stream = policy_evict_first();
-    const uint64_t pol_keep = policy_evict_last();
-    uint32_t it = 0;
-    for (int64_t r = r0; r < r1;) {
-      const int64_t l = r / M, m = r % M;
-      const int n = (int)imin64(imin64(C::ROWS, r1 - r), M - m);
-      const uint8_t* a_rows = p.a + l * p.a_sl + m * p.a_sm;
-      const uint8_t* sa_rows = p.sfa + l * p.sfa_sl + m * p.sfa_sm;
-      const uint8_t* b_l = p.b + l * p.b_sl;
-      const uint8_t* sb_l = p.sfb + l * p.sfb_sl;
-      for (int kt = 0; kt < nk; ++kt, ++it) {
-        const int s = it % C::STAGES;
-        const uint32_t ph = (it / C::STAGES) & 1;
-        if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, p.err, kDevErrTimeoutEmpty)) return;
-        const int64_t k0 = (int64_t)kt * C::KTB;
-        const uint32_t kb = (uint32_t)imin64(C::KTB, KB - k0);
-        const uint32_t fb = kb / 8;
-        const uint32_t st = sbase + s * C::STAGE_BYTES;
-        if (lane == 0) mbar_arrive_expect_tx(bar_full + 8 * s, (uint32_t)(n + 1) * (kb + fb));
-        __syncwarp();
-        if (lane < n) {
-          bulk_g2s_hint(st + lane * C::KTB, a_rows + lane * p.a_sm + k0, kb, bar_full + 8 * s, pol_stream);
-          bulk_g2s_hint(st + C::OFF_SFA + lane * C::SFB_BYTES, sa_rows + lane * p.sfa_sm + k0 / 8, fb,
-                        bar_full + 8 * s, pol_stream);
-        }
-        if (lane == 31) {
-          bulk_g2s_hint(st + C::OFF_B, b_l + k0, kb, bar_full + 8 * s, pol_keep);
-          bulk_g2s_hint(st + C::OFF_SFB, sb_l + k0 / 8, fb, bar_full + 8 * s, pol_keep);
+    // ---------------- producer: one elected thread ----------------
+    if (lane == 0) {
+      prefetch_tmap(&maps.a);
+      prefetch_tmap(&maps.sfa);
+      prefetch_tmap(&maps.b);
+      prefetch_tmap(&maps.sfb);
+      const uint64_t pol_stream = policy_evict_first();
+      const uint64_t pol_keep = policy_evict_last();
+      uint32_t it = 0;
+      for (int64_t t = t0; t < t1; ++t) {
+        const int l = (int)(t / tpl);
+        const int m0 = (int)((t % tpl) * C::ROWS);
+        for (int kt = 0; kt < nk; ++kt, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, p.err, kDevErrTimeoutEmpty)) return;
+          const uint32_t st = sbase + s * C::STAGE_BYTES;
+          const uint32_t fb = bar_full + 8 * s;
+          const int x = kt * (C::KTB / 8);  // u64 units of A == bytes of SFA
+          mbar_arrive_expect_tx(fb, C::TX);
+          tma_load_3d(st, &maps.a, fb, x, m0, l, pol_stream);
+          tma_load_3d(st + C::OFF_SFA, &maps.sfa, fb, x, m0, l, pol_stream);
+          tma_load_2d(st + C::OFF_B, &maps.b, fb, x, l, pol_keep);
+          tma_load_2d(st + C::OFF_SFB, &maps.sfb, fb, x, l, pol_keep);
         }
       }
-      r += n;
     }
     return;
   }
 
   // ---------------- consumer warps ----------------
+  const int chunk = warp % C::NCH;
+  const int group = warp / C::NCH;
+  const int off = 512 * chunk + 16 * lane;   // this lane's byte offset inside a stage row
   uint32_t it = 0;
-  for (int64_t r = r0; r < r1;) {
-    const int64_t l = r / M, m = r % M;
-    const int n = (int)imin64(imin64(C::ROWS, r1 - r), M - m);
+  int parity = 0;
+  bool dead = false;  // a wait expired: stop waiting, keep joining the named barrier
+  for (int64_t t = t0; t < t1; ++t, parity ^= 1) {
+    const int64_t l = t / tpl;
+    const int64_t m0 = (t % tpl) * C::ROWS;
     float acc[C::RPW];
 #pragma unroll
     for (int j = 0; j < C::RPW; ++j) acc[j] = 0.f;
 
     for (int kt = 0; kt < nk; ++kt, ++it) {
       const int s = it % C::STAGES;
-      const uint32_t ph = (it / C::STAGES) & 1;
-      if (!mbar_wait(bar_full + 8 * s, ph, p.err, kDevErrTimeoutFull)) return;
-      const int64_t k0 = (int64_t)kt * C::KTB;
-      const int kb = (int)imin64(C::KTB, KB - k0);
+      if (!dead && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, p.err, kDevErrTimeoutFull)) dead = true;
       const uint8_t* st = smem + s * C::STAGE_BYTES;
-
-      // b slice for this lane: chunk i at byte 512*i + 16*lane.
-      uint32_t bh[C::NCH][16];
-      float sb[C::NCH][2];
-#pragma unroll
-      for (int i = 0; i < C::NCH; ++i) {
-        const int off = 512 * i + 16 * lane;
-        if (off < kb) {
+      if constexpr (C::MODE == 0) {
+        uint32_t bh[16];
+        float sb0, sb1;
+        {
           const uint4 bv = *reinterpret_cast<const uint4*>(st + C::OFF_B + off);
-          cvt_e2m1x8(bv.x, *reinterpret_cast<uint32_t(*)[4]>(&bh[i][0]));
-          cvt_e2m1x8(bv.y, *reinterpret_cast<uint32_t(*)[4]>(&bh[i][4]));
-          cvt_e2m1x8(bv.z, *reinterpret_cast<uint32_t(*)[4]>(&bh[i][8]));
-          cvt_e2m1x8(bv.w, *reinterpret_cast<uint32_t(*)[4]>(&bh[i][12]));
+          cvt_e2m1x8(bv.x, *reinterpret_cast<uint32_t(*)[4]>(&bh[0]));
+          cvt_e2m1x8(bv.y, *reinterpret_cast<uint32_t(*)[4]>(&bh[4]));
+          cvt_e2m1x8(bv.z, *reinterpret_cast<uint32_t(*)[4]>(&bh[8]));
+          cvt_e2m1x8(bv.w, *reinterpret_cast<uint32_t(*)[4]>(&bh[12]));
           const uint32_t s2 = *reinterpret_cast<const uint16_t*>(st + C::OFF_SFB + off / 8);
-          h2_to_f2(cvt_e4m3x2(s2), sb[i][0], sb[i][1]);
+          h2_to_f2(cvt_e4m3x2(s2), sb0, sb1);
         }
-      }
-
 #pragma unroll
-      for (int j = 0; j < C::RPW; ++j) {
-        const int row = warp + j * C::CW;
-        if (row < n) {
-          const uint8_t* arow = st + row * C::KTB;
-          const uint8_t* srow = st + C::OFF_SFA + row * C::SFB_BYTES;
-#pragma unroll
-          for (int i = 0; i < C::NCH; ++i) {
-            const int off = 512 * i + 16 * lane;
-            if (off < kb) {
-              const uint4 av = *reinterpret_cast<const uint4*>(arow + off);
-              const uint32_t s2 = *reinterpret_cast<const uint16_t*>(srow + off / 8);
-              uint32_t h[4], c0 = 0u, c1 = 0u;
-              cvt_e2m1x8(av.x, h);
-              c0 = hfma2(h[0], bh[i][0], c0); c0 = hfma2(h[1], bh[i][1], c0);
-              c0 = hfma2(h[2], bh[i][2], c0); c0 = hfma2(h[3], bh[i][3], c0);
-              cvt_e2m1x8(av.y, h);
-              c0 = hfma2(h[0], bh[i][4], c0); c0 = hfma2(h[1], bh[i][5], c0);
-              c0 = hfma2(h[2], bh[i][6], c0); c0 = hfma2(h[3], bh[i][7], c0);
-              cvt_e2m1x8(av.z, h);
-              c1 = hfma2(h[0], bh[i][8], c1); c1 = hfma2(h[1], bh[i][9], c1);
-              c1 = hfma2(h[2], bh[i][10], c1); c1 = hfma2(h[3], bh[i][11], c1);
-              cvt_e2m1x8(av.w, h);
-              c1 = hfma2(h[0], bh[i][12], c1); c1 = hfma2(h[1], bh[i][13], c1);
-              c1 = hfma2(h[2], bh[i][14], c1); c1 = hfma2(h[3], bh[i][15], c1);
-              float sa0, sa1, x0, y0, x1, y1;
-              h2_to_f2(cvt_e4m3x2(s2), sa0, sa1);
-              h2_to_f2(c0, x0, y0);
-              h2_to_f2(c1, x1, y1);
-              acc[j] = fmaf(x0 + y0, sa0 * sb[i][0], acc[j]);
-              acc[j] = fmaf(x1 + y1, sa1 * sb[i][1], acc[j]);
-            }
-          }
+        for (int j = 0; j < C::RPW; ++j) {
+          const int row = group * C::RPW + j;
+          const uint4 av = *reinterpret_cast<const uint4*>(st + row * C::KTB + off);
+          const uint32_t s2 = *reinterpret_cast<const uint16_t*>(st + C::OFF_SFA + row * C::SFK + off / 8);
+          acc[j] += chunk_dot(av, s2, bh, sb0, sb1);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_empty + 8 * s);
     }
 
+    // lanes -> per-row partial of this chunk -> shared memory
+    float* rb = red + parity * C::ROWS * C::NCH;
 #pragma unroll
     for (int j = 0; j < C::RPW; ++j) {
       float v = acc[j];
 #pragma unroll
       for (int d = 16; d > 0; d >>= 1) v += __shfl_xor_sync(0xffffffffu, v, d);
-      const int row = warp + j * C::CW;
-      if (lane == 0 && row < n) p.c[l * p.c_sl + (m + row) * p.c_sm] = __float2half_rn(v);
+      if (lane == 0) rb[(group * C::RPW + j) * C::NCH + chunk] = v;
     }
-    r += n;
+    asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
+    for (int row = threadIdx.x; row < C::ROWS; row += C::CW * 32) {
+      float v = 0.f;
+#pragma unroll
+      for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
+      if (m0 + row < M) p.c[l * p.c_sl + (m0 + row) * p.c_sm] = __float2half_rn(v);
+    }
   }
 }
 
-// Plain-load kernel for shapes the bulk-copy path cannot take (K % 256 != 0 or
-// strides / pointers not 16-byte aligned).  One warp per output row; lane t
-// handles 16-element blocks t, t+32, ...; same exact per-block arithmetic.
+// Plain-load kernel for inputs the TMA path cannot take (a pointer or byte
+// stride that is not a multiple of 16).  One warp per output row; lane t
+// handles 16-element blocks t, t+32, ...; the same exact per-block arithmetic.
 __global__ void __launch_bounds__(256) gemv_generic_kernel(const __grid_constant__ GemvArgs p) {
   const int64_t warps_total = (int64_t)gridDim.x * (blockDim.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -235,9 +263,7 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const __grid_constant
     for (int64_t blk = lane; blk < nblk; blk += 32) {
       uint32_t c = 0u;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c = hfma2(cvt_e2m1x2(arow[blk * 8 + j]), cvt_e2m1x2(bl[blk * 8 + j]), c);
-      }
+      for (int j = 0; j < 8; ++j) c = hfma2(cvt_e2m1x2(arow[blk * 8 + j]), cvt_e2m1x2(bl[blk * 8 + j]), c);
       float x, y, sa, sb, d0, d1;
       h2_to_f2(c, x, y);
       h2_to_f2(cvt_e4m3x2(srow[blk]), sa, d0);
@@ -250,32 +276,146 @@ __global__ void __launch_bounds__(256) gemv_generic_kernel(const __grid_constant
   }
 }
 
+}  // namespace
+
+// Stride along L for a tensor map when L == 1 (any 16-byte multiple is valid).
+static inline uint64_t l_stride(int64_t L, int64_t given, int64_t fallback) {
+  if (L > 1) return (uint64_t)given;
+  return (uint64_t)((fallback + 15) / 16 * 16);
+}
+
+// Tensor maps depend only on the pointers, shape, strides and tile config, so
+// they are cached by value (a small LRU per process): repeated calls on the
+// same buffers skip the four driver encodes.
+struct MapKey {
+  const void* a;
+  const void* b;
+  const void* sfa;
+  const void* sfb;
+  int64_t M, K, L, a_sm, a_sl, b_sl, sfa_sm, sfa_sl, sfb_sl;
+  int cfg;
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+
+struct MapCache {
+  static constexpr int N = 16;
+  MapKey key[N];
+  GemvMaps maps[N];
+  uint64_t stamp[N] = {};
+  uint64_t clock = 0;
+  std::mutex mu;
+};
+MapCache g_map_cache;
+
 template <class C>
-int launch_tma(const GemvArgs& args, cudaStream_t stream) {
+int build_maps(const GemvArgs& p, GemvMaps& maps) {
+  const uint64_t kq = (uint64_t)(p.K / 16);  // A/b row length in u64 units == scale bytes per row
+  {
+    const uint64_t dims[3] = {kq, (uint64_t)p.M, (uint64_t)p.L};
+    const uint64_t str[2] = {(uint64_t)p.a_sm, l_stride(p.L, p.a_sl, p.a_sm * p.M)};
+    const uint32_t box[3] = {C::KTB / 8, C::ROWS, 1};
+    int rc = encode_tmap(&maps.a, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, p.a, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {kq, (uint64_t)p.M, (uint64_t)p.L};
+    const uint64_t str[2] = {(uint64_t)p.sfa_sm, l_stride(p.L, p.sfa_sl, p.sfa_sm * p.M)};
+    const uint32_t box[3] = {C::KTB / 8, C::ROWS, 1};
+    int rc = encode_tmap(&maps.sfa, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, p.sfa, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {kq, (uint64_t)p.L};
+    const uint64_t str[1] = {l_stride(p.L, p.b_sl, p.K / 2)};
+    const uint32_t box[2] = {C::KTB / 8, 1};
+    int rc = encode_tmap(&maps.b, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, p.b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[2] = {kq, (uint64_t)p.L};
+    const uint64_t str[1] = {l_stride(p.L, p.sfb_sl, p.K / 16)};
+    const uint32_t box[2] = {C::KTB / 8, 1};
+    return encode_tmap(&maps.sfb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p.sfb, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+}
+
+template <class C>
+int cached_maps(const GemvArgs& p, GemvMaps& out) {
+  MapKey k;
+  std::memset(&k, 0, sizeof(k));
+  k.a = p.a; k.b = p.b; k.sfa = p.sfa; k.sfb = p.sfb;
+  k.M = p.M; k.K = p.K; k.L = p.L;
+  k.a_sm = p.a_sm; k.a_sl = p.L > 1 ? p.a_sl : 0; k.b_sl = p.L > 1 ? p.b_sl : 0;
+  k.sfa_sm = p.sfa_sm; k.sfa_sl = p.L > 1 ? p.sfa_sl : 0; k.sfb_sl = p.L > 1 ? p.sfb_sl : 0;
+  k.cfg = C::ROWS * 1000000 + C::KTB;
+  MapCache& c = g_map_cache;
+  {
+    std::lock_guard<std::mutex> lk(c.mu);
+    for (int i = 0; i < MapCache::N; ++i)
+      if (c.stamp[i] && c.key[i] == k) {
+        c.stamp[i] = ++c.clock;
+        out = c.maps[i];
+        return NVFP4_OK;
+      }
+  }
+  int rc = build_maps<C>(p, out);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(c.mu);
+  int victim = 0;
+  for (int i = 1; i < MapCache::N; ++i)
+    if (c.stamp[i] < c.stamp[victim]) victim = i;
+  c.key[victim] = k;
+  c.maps[victim] = out;
+  c.stamp[victim] = ++c.clock;
+  return NVFP4_OK;
+}
+
+template <class C>
+int launch_tma(const GemvArgs& p, cudaStream_t stream) {
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<C>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemv)");
     attr_set[dev] = true;
   }
-  const int64_t total = args.M * args.L;
-  int64_t grid = sm_count();
-  // Small problems: keep at least one full tile per CTA.
-  const int64_t tiles = (total + C::ROWS - 1) / C::ROWS;
-  if (tiles < grid) grid = tiles;
-  if (grid < 1) grid = 1;
-  gemv_tma_kernel<C><<<(unsigned)grid, C::THREADS, C::SMEM, stream>>>(args);
+  GemvMaps maps;
+  int rc = cached_maps<C>(p, maps);
+  if (rc) return rc;
+  const int64_t ntiles = (p.M + C::ROWS - 1) / C::ROWS * p.L;
+  int64_t grid = (int64_t)sm_count() * C::MINB;
+  if (ntiles < grid) grid = ntiles;
+  gemv_tma_kernel<C><<<(unsigned)grid, C::THREADS, C::SMEM, stream>>>(maps, p);
   return check_launch("gemv_tma_kernel");
 }
 
-}  // namespace
+int launch_generic(const GemvArgs& p, cudaStream_t stream) {
+  const int64_t rows = p.M * p.L;
+  int64_t grid = (rows + 7) / 8;
+  const int64_t cap = (int64_t)sm_count() * 8;
+  if (grid > cap) grid = cap;
+  gemv_generic_kernel<<<(unsigned)grid, 256, 0, stream>>>(p);
+  return check_launch("gemv_generic_kernel");
+}
+
+// Configuration by shape: the row slice per stage matches K (one 2 KB box row
+// when K allows), and small problems use short tiles so that every SM gets
+// work.
+int gemv_dispatch(const GemvArgs& p, cudaStream_t st) {
+  const int64_t kb = p.K / 2;
+  const int64_t rows = p.M * p.L;
+  const int64_t sms = sm_count();
+  if (rows < sms * 16) {
+    if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st);
+    return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st);
+  }
+  if (kb >= 2048) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st);
+  if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st);
+  return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st);
+}
 
 }  // namespace nvfp4
-
-using nvfp4::fail;
 
 extern "C" int nvfp4_gemv(const void* a, const void* b, const void* sfa, const void* sfb, void* c,
                           int64_t M, int64_t K, int64_t L, int64_t a_sm, int64_t a_sl, int64_t b_sl,
@@ -295,17 +435,9 @@ extern "C" int nvfp4_gemv(const void* a, const void* b, const void* sfa, const v
                 device_error_word()};
   if (!args.err) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: cannot resolve the device error word");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool tma_ok = (K % 256 == 0) && aligned16(a) && aligned16(b) && aligned16(sfa) && aligned16(sfb) &&
-                      a_sm % 16 == 0 && sfa_sm % 16 == 0 && (L == 1 || (a_sl % 16 == 0 && b_sl % 16 == 0 &&
-                      sfa_sl % 16 == 0 && sfb_sl % 16 == 0));
-  if (tma_ok) {
-    using C = GemvCfg<32, 1024, 5, 8>;
-    return launch_tma<C>(args, st);
-  }
-  const int64_t rows = M * L;
-  int64_t grid = (rows + 7) / 8;
-  const int64_t cap = (int64_t)sm_count() * 8;
-  if (grid > cap) grid = cap;
-  gemv_generic_kernel<<<(unsigned)grid, 256, 0, st>>>(args);
-  return check_launch("gemv_generic_kernel");
+  const bool tma_ok = aligned16(a) && aligned16(b) && aligned16(sfa) && aligned16(sfb) && a_sm % 16 == 0 &&
+                      sfa_sm % 16 == 0 &&
+                      (L == 1 || (a_sl % 16 == 0 && b_sl % 16 == 0 && sfa_sl % 16 == 0 && sfb_sl % 16 == 0));
+  if (!tma_ok) return launch_generic(args, st);
+  return gemv_dispatch(args, st);
 }

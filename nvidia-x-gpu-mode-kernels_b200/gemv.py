@@ -24,29 +24,28 @@ _FP4_DTYPES = (torch.uint8,) + ((torch.float4_e2m1fn_x2,) if hasattr(torch, "flo
 _FP8_DTYPES = (torch.uint8, torch.float8_e4m3fn)
 
 
-def _check3(name: str, t: torch.Tensor, dtypes) -> None:
+def _check3(name: str, t, dtypes) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
     if t.dtype not in dtypes:
         raise TypeError(f"{name} has dtype {t.dtype}, expected one of {dtypes}")
     if t.dim() != 3:
         raise ValueError(f"{name} must be 3-D, got shape {tuple(t.shape)}")
-    if not t.is_cuda:
+    if t.device.type != "cuda":
         raise ValueError(f"{name} must be a CUDA tensor")
     if t.shape[1] > 1 and t.stride(1) != 1:
         raise ValueError(f"{name} must be contiguous along its second dimension, strides {t.stride()}")
 
 
 def gemv_raw(a, b, sfa, sfb, c, M: int, K: int, L: int, stream: int | None = None) -> None:
-    """Launch through the C ABI with the strides read from the tensors."""
+    """Launch through the C ABI with the strides read from the tensors (no
+    checks beyond the library's own)."""
     if stream is None:
         stream = torch.cuda.current_stream(c.device).cuda_stream
+    sa, sb, ssa, ssb, sc = a.stride(), b.stride(), sfa.stride(), sfb.stride(), c.stride()
     _lib.check(_lib.lib().nvfp4_gemv(
         a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), c.data_ptr(),
-        M, K, L,
-        a.stride(0), a.stride(2), b.stride(2),
-        sfa.stride(0), sfa.stride(2), sfb.stride(2),
-        c.stride(0), c.stride(2), stream))
+        M, K, L, sa[0], sa[2], sb[2], ssa[0], ssa[2], ssb[2], sc[0], sc[2], stream))
 
 
 def custom_kernel(a, b=None, scale_a=None, scale_b=None, c=None):
@@ -64,17 +63,21 @@ def custom_kernel(a, b=None, scale_a=None, scale_b=None, c=None):
         raise TypeError("c must be a 3-D float16 tensor [M, 1, L]")
     M, KB, L = a.shape
     K = 2 * KB
-    if b.shape[1] != KB or b.shape[2] != L or b.shape[0] < 1:
-        raise ValueError(f"b shape {tuple(b.shape)} does not match a {tuple(a.shape)}")
-    if tuple(scale_a.shape) != (M, K // 16, L):
-        raise ValueError(f"scale_a shape {tuple(scale_a.shape)}, expected {(M, K // 16, L)}")
-    if scale_b.shape[1] != K // 16 or scale_b.shape[2] != L or scale_b.shape[0] < 1:
-        raise ValueError(f"scale_b shape {tuple(scale_b.shape)} does not match K={K}, L={L}")
-    if c.shape[0] != M or c.shape[2] != L:
-        raise ValueError(f"c shape {tuple(c.shape)}, expected {(M, 1, L)}")
-    devs = {t.device for t in (a, b, scale_a, scale_b, c)}
-    if len(devs) != 1:
-        raise ValueError(f"all tensors must be on one device, got {devs}")
-    with torch.cuda.device(c.device):
+    bs, sas, sbs, cs = b.shape, scale_a.shape, scale_b.shape, c.shape
+    if bs[1] != KB or bs[2] != L or bs[0] < 1:
+        raise ValueError(f"b shape {tuple(bs)} does not match a {tuple(a.shape)}")
+    if sas[0] != M or sas[1] * 16 != K or sas[2] != L:
+        raise ValueError(f"scale_a shape {tuple(sas)}, expected {(M, K // 16, L)}")
+    if sbs[1] * 16 != K or sbs[2] != L or sbs[0] < 1:
+        raise ValueError(f"scale_b shape {tuple(sbs)} does not match K={K}, L={L}")
+    if cs[0] != M or cs[2] != L:
+        raise ValueError(f"c shape {tuple(cs)}, expected {(M, 1, L)}")
+    dev = c.device
+    if not (a.device == b.device == scale_a.device == scale_b.device == dev):
+        raise ValueError("all tensors must be on one device")
+    if dev.index != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            gemv_raw(a, b, scale_a, scale_b, c, M, K, L)
+    else:
         gemv_raw(a, b, scale_a, scale_b, c, M, K, L)
     return c

@@ -27,7 +27,9 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 def run_ref(ref, a, b, sfa, sfb, M, K, L):
     dev = torch.device("cuda")
-    perm = lambda t: torch.from_numpy(np.ascontiguousarray(t.transpose(2, 0, 1))).to(dev).permute(1, 2, 0)
+    # an explicit [L, rows, cols] copy: numpy keeps odd strides on size-1 dims,
+    # and the reference encodes the L stride even when L == 1
+    perm = lambda t: torch.from_numpy(t.transpose(2, 0, 1).copy(order="C")).contiguous().to(dev).permute(1, 2, 0)
     c = torch.empty((L, 1, M), dtype=torch.float16, device=dev).permute(2, 1, 0)
     ref.nvfp4_gemv_forward(perm(a), perm(b), perm(sfa), perm(sfb), c, M, K, L)
     torch.cuda.synchronize()

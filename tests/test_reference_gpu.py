@@ -33,5 +33,13 @@ def test_reference_vs_oracle_and_ours(pkg, oracle, cuda, ref_mod, M, K, L):
     r = c_ref.cpu().numpy().astype(np.float32)
     ours = x.c.cpu().numpy().astype(np.float32)
     cpu = oracle.gemv_torch(*(t.cpu() for t in (x.a, x.b, x.sfa, x.sfb)), M, K, L).numpy().astype(np.float32)
-    np.testing.assert_allclose(r, cpu, rtol=1e-2, atol=1e-2)      # oracle pinned to the reference
-    np.testing.assert_allclose(ours, r, rtol=1e-2, atol=1e-2)     # new kernel vs reference kernel
+    np.testing.assert_allclose(ours, cpu, rtol=1e-2, atol=1e-2)   # new kernel vs oracle (contract)
+    # The reference rounds each 32-element chunk's scaled sum in f16, so where
+    # the output cancels it can miss rtol 1e-2 by itself.  Its error is bounded
+    # relative to the output's scale, not the element: check both kernels
+    # against it at 1 % of the largest output, and 99 % of elements at 1e-2.
+    scale = np.abs(cpu).max()
+    assert np.abs(r - cpu).max() <= 1e-2 * scale
+    assert np.abs(ours - r).max() <= 1e-2 * scale
+    close = np.isclose(r, cpu, rtol=1e-2, atol=1e-2)
+    assert close.mean() >= 0.99
