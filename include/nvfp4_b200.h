@@ -90,6 +90,46 @@ NVFP4_API int nvfp4_device_errors(uint32_t* out_bits, int clear);
  */
 NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t budget_ns, void* stream);
 
+
+/*
+ * NVFP4 GEMM operands (dual and grouped GEMM): an operand with `rows` rows is
+ *   codes   [rows, K/2] bytes, row stride ld (bytes, a multiple of 16), K-major;
+ *   scales  e4m3 (unsigned: sign bit 0), one per 16 K-elements, in the 128x4
+ *           blocked layout: 128-row x 4-column tiles of 512 bytes, row-tile
+ *           major; inside a tile the scale of (row r, block c) sits at byte
+ *           (r % 32) * 16 + (r / 32 % 4) * 4 + c % 4; rows padded to 128 and
+ *           K/16 to a multiple of 4 with zeros.
+ * K must be a multiple of 64; pointers 16-byte aligned.  Outputs are fp16,
+ * row stride ldc elements (a multiple of 8).  No counterpart exists in the
+ * reference, which ships only the GEMV and announces a dual GEMM
+ * (Nvidia-x-GPU-MODE-Kernels README.md:3); the contract is
+ * fp32 accumulation of the dequantised products, one rounding to fp16.
+ */
+
+/* out[M, N] = silu(A . B1^T) * (A . B2^T); B1, B2 are [N, K/2] with row stride ldb. */
+NVFP4_API int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2,
+                              const void* sfa, const void* sfb1, const void* sfb2, void* out,
+                              int64_t M, int64_t N, int64_t K,
+                              int64_t lda, int64_t ldb, int64_t ldc, void* stream);
+
+/* One problem of a grouped GEMM: c[M, N] = a[M, K] . b[N, K]^T. */
+typedef struct nvfp4_group {
+  const void* a;
+  const void* b;
+  const void* sfa;
+  const void* sfb;
+  void* c;
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc;
+} nvfp4_group;
+
+/*
+ * Grouped GEMM over `num_groups` independent problems (host array of
+ * descriptors; groups with M == 0 are skipped).  One persistent launch covers
+ * up to 32 groups; its CTAs walk the tiles of all groups.
+ */
+NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,8 +5,11 @@ directory name is not a Python identifier).
 
 * ``gemv.custom_kernel(a, b, scale_a, scale_b, c)`` - batched block-scaled GEMV,
   the operator of the reference (blackwell_nvfp4_gemv.cu:500-524).
+* ``dual_gemm(a, b1, b2, scale_a, scale_b1, scale_b2, c)`` - silu(a.b1^T)*(a.b2^T).
+* ``grouped_gemm(a_list, b_list, scale_a_list, scale_b_list, c_list)``.
 """
-from . import _lib, gemv, inputs, layout, sharded  # noqa: F401
+from . import _lib, gemm, gemv, inputs, layout, sharded  # noqa: F401
+from .gemm import dual_gemm, grouped_gemm  # noqa: F401
 from .gemv import custom_kernel  # noqa: F401
 
-__all__ = ["custom_kernel", "gemv", "inputs", "layout"]
+__all__ = ["custom_kernel", "dual_gemm", "grouped_gemm", "gemm", "gemv", "inputs", "layout", "sharded"]

@@ -20,12 +20,20 @@ _lib = None
 I64 = ctypes.c_int64
 VP = ctypes.c_void_p
 
+class Group(ctypes.Structure):
+    """struct nvfp4_group (include/nvfp4_b200.h)."""
+    _fields_ = [("a", VP), ("b", VP), ("sfa", VP), ("sfb", VP), ("c", VP),
+                ("M", I64), ("N", I64), ("K", I64), ("lda", I64), ("ldb", I64), ("ldc", I64)]
+
+
 # name -> argtypes; every entry point returns int (status).
 SIGNATURES: dict[str, list] = {
     "nvfp4_gemv": [VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_device_errors": [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int],
     "nvfp4_selftest_wait_timeout": [ctypes.c_uint64, VP],
     "nvfp4_version": [],
+    "nvfp4_dual_gemm": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, VP],
+    "nvfp4_grouped_gemm": [ctypes.POINTER(Group), ctypes.c_int, VP],
 }
 
 STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "ALIGNMENT", 3: "CUDA", 4: "TIMEOUT", 5: "UNSUPPORTED"}

@@ -1,0 +1,411 @@
+// NVFP4 block-scaled GEMMs on the tcgen05 tensor cores (sm_100a):
+//
+//   grouped:  C_g[M_g, N_g] = A_g[M_g, K_g] . B_g[N_g, K_g]^T          (fp16 out)
+//   dual:     C[M, N] = silu(A . B1^T) * (A . B2^T)                    (fp16 out)
+//
+// Operands are e2m1 codes packed two per byte, K-major (rows of K/2 bytes),
+// with one e4m3 scale per 16 K-elements stored in the 128x4 blocked layout
+// (128-row x 4-scale tiles of 512 bytes, row-tile major; inside a tile the
+// scale (r, c) sits at byte (r%32)*16 + (r/32)*4 + c).  That layout is what a
+// tcgen05.cp 32x128b.warpx4 copy turns into the tensor-memory arrangement the
+// block-scaled MMA reads, so scales go global -> shared -> tensor memory with
+// plain copies.  The MMA reads scales as unsigned e4m3 (sign bit must be 0).
+//
+// One persistent CTA per SM walks output tiles of 128 x BN (tile t, t+grid,
+// ...).  Tiles of a group are ordered M-tile fastest, so CTAs running at the
+// same time share B tiles through L2.  Warp roles:
+//   warp 0  TMA producer: per 256-element K step, one 128x128-byte box of A and
+//           one BNx128-byte box of B (and B2) with 128-byte swizzle, plus 1-D
+//           bulk copies of the 2 KB scale blocks, into a STAGES-deep ring;
+//   warp 1  allocates tensor memory; one thread copies the stage's scales into
+//           tensor memory and issues 4 MMAs of K=64 (kind::mxf4nvf4,
+//           scale_vec::4X) per B operand, then commits the stage back to the
+//           producer and, after the last K step, the accumulator to the
+//           epilogue;
+//   warps 2-5  epilogue: tcgen05.ld of the fp32 accumulator rows (one row per
+//           thread), SiLU-gate or plain conversion to fp16, 16-byte stores.
+// Every mbarrier wait is bounded (2 s) and reports into the device error word.
+#include <cuda_fp16.h>
+#include <cstring>
+#include <mutex>
+#include "ptx.cuh"
+#include "tcgen05.cuh"
+#include "common.h"
+#include "tmap.h"
+
+namespace nvfp4 {
+namespace {
+
+constexpr int BM = 128;          // rows per tile (one MMA of M=128)
+constexpr int KSTEP = 256;       // K elements per stage = 128 bytes per row
+constexpr int KSTEP_BYTES = 128;
+
+struct GemmGroup {
+  CUtensorMap ta, tb, tb2;       // A [M, K/2], B [N, K/2] (B2 for the dual GEMM)
+  const uint8_t* sfa;            // blocked scales of A, B, B2
+  const uint8_t* sfb;
+  const uint8_t* sfb2;
+  __half* c;
+  int64_t ldc;                   // elements
+  int M, N, K;
+  int tiles_m, tiles_n, tile_begin;
+};
+
+template <int MAXG>
+struct GemmParams {
+  GemmGroup g[MAXG];
+  int ngroups;
+  int total_tiles;
+  uint32_t* err;
+};
+
+template <int BN_, bool DUAL_, int STAGES_>
+struct GemmCfg {
+  static constexpr int BN = BN_;
+  static constexpr bool DUAL = DUAL_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int NB = BN / 128;                      // 128-row scale blocks per B tile
+  static constexpr int A_BYTES = BM * KSTEP_BYTES;         // 16 KB
+  static constexpr int B_BYTES = BN * KSTEP_BYTES;
+  static constexpr int SFA_BYTES = 4 * 512;                // 4 K-blocks of 64
+  static constexpr int SFB_BYTES = NB * 4 * 512;
+  static constexpr int OFF_B = A_BYTES;
+  static constexpr int OFF_B2 = OFF_B + B_BYTES;
+  static constexpr int OFF_SFA = OFF_B2 + (DUAL ? B_BYTES : 0);
+  static constexpr int OFF_SFB = OFF_SFA + SFA_BYTES;
+  static constexpr int OFF_SFB2 = OFF_SFB + SFB_BYTES;
+  static constexpr int STAGE_BYTES = ((OFF_SFB2 + (DUAL ? SFB_BYTES : 0)) + 1023) / 1024 * 1024;
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int SMEM = OFF_BAR + (2 * STAGES + 4) * 8 + 16 + 1024;  // + 1 KB alignment slack
+  // tensor memory columns
+  static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
+  static constexpr int SF_BASE = ACC_COLS;
+  static constexpr int SFB_COLS_PER_KB = NB * 4;
+  static constexpr int SF_STAGE_COLS = 16 + 4 * SFB_COLS_PER_KB + (DUAL ? 4 * SFB_COLS_PER_KB : 0);
+  static constexpr int TMEM_COLS = 512;
+  static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+  static constexpr int THREADS = 192;
+  static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(BM, BN);
+};
+
+__device__ __forceinline__ int find_group(const GemmGroup* g, int ng, int t) {
+  int i = 0;
+  while (i + 1 < ng && g[i + 1].tile_begin <= t) ++i;
+  return i;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <class C, int MAXG>
+__global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams<MAXG> P) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t bar_full = sbase + C::OFF_BAR;
+  const uint32_t bar_empty = bar_full + 8 * C::STAGES;
+  const uint32_t bar_accf = bar_empty + 8 * C::STAGES;
+  const uint32_t bar_acce = bar_accf + 8;
+  const uint32_t bar_done = bar_acce + 8;
+  const uint32_t tmem_slot = bar_done + 8;
+  volatile uint32_t* tmem_slot_ptr =
+      reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_accf, 1);
+    mbar_init(bar_acce, 4);
+    mbar_init(bar_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    // ---------------------------- producer ----------------------------
+    if (lane == 0) {
+      for (int i = 0; i < P.ngroups; ++i) {
+        prefetch_tmap(&P.g[i].ta);
+        prefetch_tmap(&P.g[i].tb);
+        if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
+      }
+      const uint64_t pol_a = policy_evict_last();   // A tiles are re-read by every N tile
+      const uint64_t pol_b = policy_evict_first();  // B tiles stream (shared only by concurrent CTAs)
+      uint32_t it = 0;
+      for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
+        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+        const int local = t - G.tile_begin;
+        const int mt = local % G.tiles_m, nt = local / G.tiles_m;
+        const int nk64 = G.K / 64;
+        const int nks = (nk64 + 3) / 4;
+        const int nrt_b = (G.N + 127) / 128;
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
+          const uint32_t st = sbase + s * C::STAGE_BYTES;
+          const uint32_t fb = bar_full + 8 * s;
+          const int nch = min(4, nk64 - 4 * ks);
+          int nbv = 0;
+          for (int nb = 0; nb < C::NB; ++nb) nbv += (nt * C::NB + nb < nrt_b) ? 1 : 0;
+          const uint32_t sfb_bytes = (uint32_t)(nbv * nch * 512);
+          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) + nch * 512 +
+                                 sfb_bytes * (C::DUAL ? 2 : 1);
+          mbar_arrive_expect_tx(fb, bytes);
+          tma_load_2d(st, &G.ta, fb, ks * KSTEP_BYTES, mt * BM, pol_a);
+          tma_load_2d(st + C::OFF_B, &G.tb, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
+          if (C::DUAL) tma_load_2d(st + C::OFF_B2, &G.tb2, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
+          bulk_g2s(st + C::OFF_SFA, G.sfa + ((size_t)mt * nk64 + 4 * ks) * 512, nch * 512, fb);
+          for (int nb = 0; nb < C::NB; ++nb) {
+            const int rt = nt * C::NB + nb;
+            if (rt >= nrt_b) continue;
+            bulk_g2s(st + C::OFF_SFB + nb * 2048, G.sfb + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, fb);
+            if (C::DUAL)
+              bulk_g2s(st + C::OFF_SFB2 + nb * 2048, G.sfb2 + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, fb);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA -------------------------------
+    if (lane == 0) {
+      uint32_t it = 0, tile_it = 0;
+      for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
+        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+        const int nk64 = G.K / 64;
+        const int nks = (nk64 + 3) / 4;
+        if (!mbar_wait(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
+        tc::fence_after_sync();
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
+          tc::fence_after_sync();
+          const uint32_t st = sbase + s * C::STAGE_BYTES;
+          const int nch = min(4, nk64 - 4 * ks);
+          const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
+          const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFB_COLS_PER_KB;
+          for (int kk = 0; kk < nch; ++kk) {
+            tc::cp_sf_32x128b_x4(sfa_t + 4 * kk, tc::desc_sf_block(st + C::OFF_SFA + kk * 512));
+            for (int nb = 0; nb < C::NB; ++nb) {
+              tc::cp_sf_32x128b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
+                                   tc::desc_sf_block(st + C::OFF_SFB + nb * 2048 + kk * 512));
+              if (C::DUAL)
+                tc::cp_sf_32x128b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
+                                     tc::desc_sf_block(st + C::OFF_SFB2 + nb * 2048 + kk * 512));
+            }
+          }
+          const uint64_t da = tc::desc_sw128(st), db = tc::desc_sw128(st + C::OFF_B);
+          const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
+          for (int kk = 0; kk < nch; ++kk) {
+            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+            // the k-th 64-element slice starts 32 bytes further (encoded >> 4)
+            tc::mma_mxf4nvf4(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk,
+                             sfb_t + kk * C::SFB_COLS_PER_KB, accum);
+            if (C::DUAL)
+              tc::mma_mxf4nvf4(tmem + C::BN, da + 2 * kk, db2 + 2 * kk, C::IDESC, sfa_t + 4 * kk,
+                               sfb2_t + kk * C::SFB_COLS_PER_KB, accum);
+          }
+          tc::commit(bar_empty + 8 * s);
+        }
+        tc::commit(bar_accf);
+      }
+    }
+  } else {
+    // ---------------------------- epilogue ----------------------------
+    const int sub = warp & 3;                 // tensor-memory lane quarter of this warp
+    const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
+    uint32_t tile_it = 0;
+    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
+      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+      const int local = t - G.tile_begin;
+      const int mt = local % G.tiles_m, nt = local / G.tiles_m;
+      if (!mbar_wait(bar_accf, tile_it & 1, P.err, kDevErrTimeoutMma)) break;
+      tc::fence_after_sync();
+      const int row = mt * BM + sub * 32 + lane;
+      __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
+#pragma unroll 1
+      for (int cb = 0; cb < C::BN / 32; ++cb) {
+        uint32_t v[32];
+        tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
+        uint32_t h[16];
+        if constexpr (C::DUAL) {
+          uint32_t u[32];
+          tc::ld_32x32b_x32(tmem + lane_base + C::BN + cb * 32, u);
+          tc::wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            h[j] = pack_h2(silu_mul(__uint_as_float(v[2 * j]), __uint_as_float(u[2 * j])),
+                           silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
+        } else {
+          tc::wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) h[j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+        }
+        const int col0 = nt * C::BN + cb * 32;
+        if (row < G.M) {
+          if (col0 + 32 <= G.N) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + cb * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+          } else {
+            const __half* hs = reinterpret_cast<const __half*>(h);
+            for (int j = 0; j < 32 && col0 + j < G.N; ++j) crow[cb * 32 + j] = hs[j];
+          }
+        }
+      }
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_acce);
+    }
+  }
+done:
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+namespace {
+
+template <class C, int MAXG>
+int launch_gemm(const GemmParams<MAXG>& P, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<C, MAXG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm)");
+    attr_set[dev] = true;
+  }
+  int grid = sm_count();
+  if (P.total_tiles < grid) grid = P.total_tiles;
+  if (grid < 1) return NVFP4_OK;
+  gemm_kernel<C, MAXG><<<grid, C::THREADS, C::SMEM, stream>>>(P);
+  return check_launch("gemm_kernel");
+}
+
+int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+  const uint64_t dims[2] = {(uint64_t)(K / 2), (uint64_t)rows};
+  const uint64_t str[1] = {(uint64_t)ld};
+  const uint32_t box[2] = {KSTEP_BYTES, (uint32_t)box_rows};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int check_operand(const char* name, const void* p, const void* sf, int64_t rows, int64_t K, int64_t ld) {
+  if (!p || !sf) return fail(NVFP4_ERR_INVALID, "%s: null pointer", name);
+  if (rows < 1) return fail(NVFP4_ERR_INVALID, "%s: need at least one row", name);
+  if (ld < K / 2) return fail(NVFP4_ERR_INVALID, "%s: row stride %lld below K/2", name, (long long)ld);
+  if (!aligned16(p) || !aligned16(sf) || ld % 16)
+    return fail(NVFP4_ERR_ALIGNMENT, "%s: pointers and row stride must be multiples of 16 bytes", name);
+  return NVFP4_OK;
+}
+
+int check_out(void* c, int64_t N, int64_t ldc) {
+  if (!c) return fail(NVFP4_ERR_INVALID, "output: null pointer");
+  if (ldc < N) return fail(NVFP4_ERR_INVALID, "output: ldc below N");
+  if (!aligned16(c) || ldc % 8)
+    return fail(NVFP4_ERR_ALIGNMENT, "output: pointer must be 16-byte aligned and ldc a multiple of 8");
+  return NVFP4_OK;
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+using namespace nvfp4;
+
+extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa, const void* sfb1,
+                               const void* sfb2, void* c, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, int64_t ldc, void* stream) {
+  using C = GemmCfg<128, true, 4>;
+  if (K < 64 || K % 64) return fail(NVFP4_ERR_INVALID, "nvfp4_dual_gemm: K must be a positive multiple of 64");
+  int rc;
+  if ((rc = check_operand("a", a, sfa, M, K, lda)) || (rc = check_operand("b1", b1, sfb1, N, K, ldb)) ||
+      (rc = check_operand("b2", b2, sfb2, N, K, ldb)) || (rc = check_out(c, N, ldc)))
+    return rc;
+  GemmParams<1> P;
+  std::memset(&P, 0, sizeof(P));
+  GemmGroup& G = P.g[0];
+  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::BN)) ||
+      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::BN)))
+    return rc;
+  G.sfa = static_cast<const uint8_t*>(sfa);
+  G.sfb = static_cast<const uint8_t*>(sfb1);
+  G.sfb2 = static_cast<const uint8_t*>(sfb2);
+  G.c = static_cast<__half*>(c);
+  G.ldc = ldc;
+  G.M = (int)M; G.N = (int)N; G.K = (int)K;
+  G.tiles_m = (int)((M + BM - 1) / BM);
+  G.tiles_n = (int)((N + C::BN - 1) / C::BN);
+  G.tile_begin = 0;
+  P.ngroups = 1;
+  P.total_tiles = G.tiles_m * G.tiles_n;
+  P.err = device_error_word();
+  if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_dual_gemm: cannot resolve the device error word");
+  return launch_gemm<C, 1>(P, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream) {
+  using C = GemmCfg<256, false, 4>;
+  constexpr int MAXG = 32;
+  if (!groups || num_groups < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_grouped_gemm: no groups");
+  uint32_t* err = device_error_word();
+  if (!err) return fail(NVFP4_ERR_CUDA, "nvfp4_grouped_gemm: cannot resolve the device error word");
+  static GemmParams<MAXG> P;          // large; built under a lock, copied into the launch
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int g0 = 0; g0 < num_groups; g0 += MAXG) {
+    std::memset(&P, 0, sizeof(P));
+    int tiles = 0, n = 0;
+    for (int i = g0; i < num_groups && n < MAXG; ++i) {
+      const nvfp4_group& q = groups[i];
+      if (q.M == 0) continue;
+      int rc;
+      if (q.K < 64 || q.K % 64 || q.N < 1 || q.M < 0)
+        return fail(NVFP4_ERR_INVALID, "group %d: need M>=0, N>=1 and K a positive multiple of 64", i);
+      if ((rc = check_operand("a", q.a, q.sfa, q.M, q.K, q.lda)) ||
+          (rc = check_operand("b", q.b, q.sfb, q.N, q.K, q.ldb)) || (rc = check_out(q.c, q.N, q.ldc)))
+        return rc;
+      GemmGroup& G = P.g[n];
+      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::BN)))
+        return rc;
+      G.sfa = static_cast<const uint8_t*>(q.sfa);
+      G.sfb = static_cast<const uint8_t*>(q.sfb);
+      G.c = static_cast<__half*>(q.c);
+      G.ldc = q.ldc;
+      G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
+      G.tiles_m = (int)((q.M + BM - 1) / BM);
+      G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
+      G.tile_begin = tiles;
+      tiles += G.tiles_m * G.tiles_n;
+      ++n;
+    }
+    if (n == 0) continue;
+    P.ngroups = n;
+    P.total_tiles = tiles;
+    P.err = err;
+    int rc = launch_gemm<C, MAXG>(P, static_cast<cudaStream_t>(stream));
+    if (rc) return rc;
+  }
+  return NVFP4_OK;
+}
