@@ -99,8 +99,9 @@ NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t budget_ns, void* stream);
  *           major; inside a tile the scale of (row r, block c) sits at byte
  *           (r % 32) * 16 + (r / 32 % 4) * 4 + c % 4; rows padded to 128 and
  *           K/16 to a multiple of 4 with zeros.
- * K must be a multiple of 64; pointers 16-byte aligned.  Outputs are fp16,
- * row stride ldc elements (a multiple of 8).  No counterpart exists in the
+ * K must be a multiple of 64; operand pointers 16-byte aligned.  Outputs are
+ * fp16 with row stride ldc elements (16-byte stores when the pointer is 16-byte
+ * aligned and ldc % 8 == 0, element stores otherwise).  No counterpart exists in the
  * reference, which ships only the GEMV and announces a dual GEMM
  * (Nvidia-x-GPU-MODE-Kernels README.md:3); the contract is
  * fp32 accumulation of the dequantised products, one rounding to fp16.
@@ -129,6 +130,14 @@ typedef struct nvfp4_group {
  * up to 32 groups; its CTAs walk the tiles of all groups.
  */
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
+
+/*
+ * Tensor-core peak probe: one CTA per SM issues `iters` dense 128x256x64
+ * kind::mxf4nvf4 MMAs (4,194,304 FLOP each) from shared memory.  Time it with
+ * events on `stream` to get the device's FP4 tensor throughput, the
+ * denominator of the GEMMs' roofline fraction.  No counterpart in the reference.
+ */
+NVFP4_API int nvfp4_mma_peak(int iters, void* stream);
 
 #ifdef __cplusplus
 }

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, list] = {
     "nvfp4_version": [],
     "nvfp4_dual_gemm": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_grouped_gemm": [ctypes.POINTER(Group), ctypes.c_int, VP],
+    "nvfp4_mma_peak": [ctypes.c_int, VP],
 }
 
 STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "ALIGNMENT", 3: "CUDA", 4: "TIMEOUT", 5: "UNSUPPORTED"}

@@ -49,6 +49,7 @@ struct GemmGroup {
   int64_t ldc;                   // elements
   int M, N, K;
   int tiles_m, tiles_n, tile_begin;
+  int vec_ok;                    // c 16-byte aligned and ldc % 8 == 0: 16-byte stores
 };
 
 template <int MAXG>
@@ -260,7 +261,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         }
         const int col0 = nt * C::BN + cb * 32;
         if (row < G.M) {
-          if (col0 + 32 <= G.N) {
+          if (col0 + 32 <= G.N && G.vec_ok) {
             uint4* dst = reinterpret_cast<uint4*>(crow + cb * 32);
 #pragma unroll
             for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
@@ -324,10 +325,11 @@ int check_operand(const char* name, const void* p, const void* sf, int64_t rows,
 int check_out(void* c, int64_t N, int64_t ldc) {
   if (!c) return fail(NVFP4_ERR_INVALID, "output: null pointer");
   if (ldc < N) return fail(NVFP4_ERR_INVALID, "output: ldc below N");
-  if (!aligned16(c) || ldc % 8)
-    return fail(NVFP4_ERR_ALIGNMENT, "output: pointer must be 16-byte aligned and ldc a multiple of 8");
+  if (reinterpret_cast<uintptr_t>(c) & 1) return fail(NVFP4_ERR_ALIGNMENT, "output: fp16 pointer not 2-byte aligned");
   return NVFP4_OK;
 }
+
+int vec_ok(const void* c, int64_t ldc) { return aligned16(c) && ldc % 8 == 0; }
 
 }  // namespace
 }  // namespace nvfp4
@@ -354,6 +356,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   G.sfb2 = static_cast<const uint8_t*>(sfb2);
   G.c = static_cast<__half*>(c);
   G.ldc = ldc;
+  G.vec_ok = vec_ok(c, ldc);
   G.M = (int)M; G.N = (int)N; G.K = (int)K;
   G.tiles_m = (int)((M + BM - 1) / BM);
   G.tiles_n = (int)((N + C::BN - 1) / C::BN);
@@ -393,6 +396,7 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
       G.sfb = static_cast<const uint8_t*>(q.sfb);
       G.c = static_cast<__half*>(q.c);
       G.ldc = q.ldc;
+      G.vec_ok = vec_ok(q.c, q.ldc);
       G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
       G.tiles_m = (int)((q.M + BM - 1) / BM);
       G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
@@ -408,4 +412,65 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
     if (rc) return rc;
   }
   return NVFP4_OK;
+}
+
+// ---------------------------------------------------------------------------
+// FP4 tensor-core peak probe: every CTA (one per SM) issues `iters` dense
+// 128x256x64 kind::mxf4nvf4 MMAs back to back from shared memory into one
+// tensor-memory accumulator, with nothing else in the loop.  The operand bytes
+// are whatever shared memory holds; only the issue rate matters.  It gives the
+// denominator of the GEMMs' tensor-core roofline fraction.
+// ---------------------------------------------------------------------------
+namespace {
+__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, uint32_t* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  const uint32_t bar = sbase + 49152;
+  const uint32_t slot = bar + 8;
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem_raw + (slot - raw));
+  if (threadIdx.x == 0) {
+    const uint64_t da = tc::desc_sw128(sbase), db = tc::desc_sw128(sbase + 16384);
+    const uint32_t idesc = tc::idesc_mxf4nvf4(128, 256);
+    for (int i = 0; i < iters; ++i)
+      tc::mma_mxf4nvf4(tmem, da + 2 * (i & 3), db + 2 * (i & 3), idesc, tmem + 256, tmem + 272, i > 0 ? 1u : 0u);
+    tc::commit(bar);
+    mbar_wait(bar, 0, err, kDevErrTimeoutMma);
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+}  // namespace
+
+extern "C" int nvfp4_mma_peak(int iters, void* stream) {
+  if (iters < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_mma_peak: iters must be positive");
+  uint32_t* err = device_error_word();
+  if (!err) return fail(NVFP4_ERR_CUDA, "nvfp4_mma_peak: cannot resolve the device error word");
+  constexpr int kSmem = 49152 + 64 + 1024;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(mma_peak_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mma_peak)");
+    attr_set[dev] = true;
+  }
+  mma_peak_kernel<<<sm_count(), 128, kSmem, static_cast<cudaStream_t>(stream)>>>(iters, err);
+  return check_launch("mma_peak_kernel");
 }
