@@ -421,6 +421,7 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
 // are whatever shared memory holds; only the issue rate matters.  It gives the
 // denominator of the GEMMs' tensor-core roofline fraction.
 // ---------------------------------------------------------------------------
+namespace nvfp4 {
 namespace {
 __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
@@ -457,6 +458,7 @@ __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, uint32_t* e
   }
 }
 }  // namespace
+}  // namespace nvfp4
 
 extern "C" int nvfp4_mma_peak(int iters, void* stream) {
   if (iters < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_mma_peak: iters must be positive");
