@@ -249,6 +249,64 @@ def run_gemv_extra(pkg, flush, M, K, L, steps, warmup):
             "us_median": round(statistics.median(ts) * 1e3, 3)}
 
 
+def fp4_peak_tflops(pkg, iters=4096, reps=5):
+    """Dense FP4 tensor throughput measured with the library's MMA probe."""
+    lib = pkg._lib.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    pkg._lib.check(lib.nvfp4_mma_peak(iters, stream))
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        pkg._lib.check(lib.nvfp4_mma_peak(iters, stream))
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    return sms * iters * 2 * 128 * 256 * 64 / (min(ts) * 1e-3) / 1e12
+
+
+def run_dual_extra(pkg, flush, steps, warmup, peak_tf, hbm):
+    M, N, K = 256, 14336, 4096
+    g = torch.Generator().manual_seed(0)
+    x, w1, w2 = (pkg.inputs.operand(r, K, g, device="cuda") for r in (M, N, N))
+    c = torch.empty((M, N), dtype=torch.float16, device="cuda")
+
+    def step(ev):
+        ev_mark(ev)
+        pkg.dual_gemm(x.codes, w1.codes, w2.codes, x.sf_blocked, w1.sf_blocked, w2.sf_blocked, c)
+        ev_mark(ev)
+
+    t = statistics.mean(s[0] for s in time_steps(step, steps, warmup, flush)) * 1e-3
+    flop = 2 * 2 * M * N * K
+    nbytes = (M + 2 * N) * K // 2 + (M + 2 * N) * K // 16 + 2 * M * N
+    return {"workload": f"dual gemm silu(XW1)*(XW2) M={M} N={N} K={K}", "us": round(t * 1e6, 3),
+            "tflops": round(flop / t / 1e12, 1), "fp4_peak_frac": round(flop / t / 1e12 / peak_tf, 4),
+            "gbs": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4)}
+
+
+def run_grouped_extra(pkg, flush, steps, warmup, peak_tf, hbm):
+    N, K = 4096, 7168
+    Ms = pkg.inputs.grouped_m_sizes(8, seed=0)
+    g = torch.Generator().manual_seed(0)
+    As = [pkg.inputs.operand(m, K, g, device="cuda") for m in Ms]
+    Bs = [pkg.inputs.operand(N, K, g, device="cuda") for _ in Ms]
+    cs = [torch.empty((m, N), dtype=torch.float16, device="cuda") for m in Ms]
+    args = ([a.codes for a in As], [b.codes for b in Bs], [a.sf_blocked for a in As], [b.sf_blocked for b in Bs], cs)
+
+    def step(ev):
+        ev_mark(ev)
+        pkg.grouped_gemm(*args)
+        ev_mark(ev)
+
+    t = statistics.mean(s[0] for s in time_steps(step, steps, warmup, flush)) * 1e-3
+    flop = 2 * sum(Ms) * N * K
+    nbytes = sum((m + N) * K // 2 + (m + N) * K // 16 + 2 * m * N for m in Ms)
+    return {"workload": f"grouped gemm G=8 M={Ms} N={N} K={K}", "us": round(t * 1e6, 3),
+            "tflops": round(flop / t / 1e12, 1), "fp4_peak_frac": round(flop / t / 1e12 / peak_tf, 4),
+            "gbs": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4)}
+
+
 def our_arm(args, world, rank, local):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
@@ -344,6 +402,11 @@ def our_arm(args, world, rank, local):
                               run_gemv_extra(pkg, flush, 4096, 14336, 8, 20, 3)]
             for e in line["extras"]:
                 e["hbm_frac"] = round(e["gbs"] / pk["hbm_gbs"], 4)
+            peak_tf = fp4_peak_tflops(pkg)
+            line["fp4_peak_tflops_measured"] = round(peak_tf, 1)
+            line["extras"] += [run_dual_extra(pkg, flush, 30, 3, peak_tf, pk["hbm_gbs"]),
+                               run_grouped_extra(pkg, flush, 20, 3, peak_tf, pk["hbm_gbs"])]
+            line["gpu_launches_extras_note"] = "extras are separate timed loops, not part of gpu_launches"
     return line
 
 

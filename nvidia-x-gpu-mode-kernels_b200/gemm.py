@@ -91,9 +91,12 @@ def grouped_gemm(a_list, b_list, scale_a_list, scale_b_list, c_list):
     for i in range(G):
         a, b, c = _codes(f"a[{i}]", a_list[i]), _codes(f"b[{i}]", b_list[i]), c_list[i]
         M, K, N = a.shape[0], a.shape[1] * 2, b.shape[0]
+        if M == 0:   # empty group: the library skips it
+            arr[i] = _lib.Group(None, None, None, None, None, 0, N, K, 0, 0, 0)
+            continue
         if b.shape[1] * 2 != K:
             raise ValueError(f"group {i}: a and b disagree on K")
-        sa = _scales(f"scale_a[{i}]", scale_a_list[i], max(M, 1), K)
+        sa = _scales(f"scale_a[{i}]", scale_a_list[i], M, K)
         sb = _scales(f"scale_b[{i}]", scale_b_list[i], N, K)
         _out(c, M, N)
         keep += [sa, sb]
