@@ -479,8 +479,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--profile", action="store_true",
-                    help="run only the headline kernel (warmup + steps launches) for ncu captures")
+    ap.add_argument("--profile", nargs="?", const="gemv", default=None, choices=["gemv", "dual", "grouped"],
+                    help="run only one kernel (warmup + steps launches) for ncu captures")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -488,9 +488,15 @@ def main():
     if args.profile:
         import __graft_entry__
         pkg = __graft_entry__.load_package()
-        x = pkg.inputs.gemv_inputs(HEADLINE["M"], HEADLINE["K"], HEADLINE["L"], seed=0, device="cuda")
-        for _ in range(args.warmup + args.steps):
-            pkg.custom_kernel(*x.as_tuple())
+        noflush = lambda: None
+        if args.profile == "gemv":
+            x = pkg.inputs.gemv_inputs(HEADLINE["M"], HEADLINE["K"], HEADLINE["L"], seed=0, device="cuda")
+            for _ in range(args.warmup + args.steps):
+                pkg.custom_kernel(*x.as_tuple())
+        elif args.profile == "dual":
+            run_dual_extra(pkg, noflush, args.steps, args.warmup, 1.0, 1.0)
+        else:
+            run_grouped_extra(pkg, noflush, args.steps, args.warmup, 1.0, 1.0)
         torch.cuda.synchronize()
         print(json.dumps({"profile_run": "ok", "launches": args.warmup + args.steps}))
         return
