@@ -42,6 +42,7 @@ constexpr int KSTEP_BYTES = 128;
 
 struct GemmGroup {
   CUtensorMap ta, tb, tb2;       // A [M, K/2], B [N, K/2] (B2 for the dual GEMM)
+  CUtensorMap tc;                // C [M, N] fp16, 64-column boxes, 128-byte swizzle
   const uint8_t* sfa;            // blocked scales of A, B, B2
   const uint8_t* sfb;
   const uint8_t* sfb2;
@@ -50,6 +51,7 @@ struct GemmGroup {
   int M, N, K;
   int tiles_m, tiles_n, tile_begin;
   int vec_ok;                    // c 16-byte aligned and ldc % 8 == 0: 16-byte stores
+  int tma_store;                 // tc is valid: the epilogue stores through shared memory + TMA
 };
 
 template <int MAXG>
@@ -60,8 +62,20 @@ struct GemmParams {
   uint32_t* err;
 };
 
-template <int BN_, bool DUAL_, int STAGES_>
+// DBG is a tuning knob (0 in every product instantiation): bit 0 skips the
+// scale copies, bit 1 the MMAs, bit 2 the loads, bit 3 the epilogue's
+// tensor-memory loads and stores, to time each link alone.
+// SFST selects how block scales reach tensor memory: 0 = tcgen05.cp issued by
+// the MMA thread, 1 = four scale warps that tcgen05.st them (off the MMA queue).
+// EPI 1 stages the fp16 tile in shared memory and writes it with TMA stores
+// (needs BM*BN*2 bytes of shared memory); EPI 0 stores rows from registers.
+// POL picks the L2 policy of B loads: 0 evict-first, 1 normal.
+template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0>
 struct GemmCfg {
+  static constexpr int DBG = DBG_;
+  static constexpr int EPI = EPI_;
+  static constexpr int POL = POL_;
+  static constexpr int SFST = SFST_;
   static constexpr int BN = BN_;
   static constexpr bool DUAL = DUAL_;
   static constexpr int STAGES = STAGES_;
@@ -76,8 +90,10 @@ struct GemmCfg {
   static constexpr int OFF_SFB = OFF_SFA + SFA_BYTES;
   static constexpr int OFF_SFB2 = OFF_SFB + SFB_BYTES;
   static constexpr int STAGE_BYTES = ((OFF_SFB2 + (DUAL ? SFB_BYTES : 0)) + 1023) / 1024 * 1024;
-  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-  static constexpr int SMEM = OFF_BAR + (2 * STAGES + 4) * 8 + 16 + 1024;  // + 1 KB alignment slack
+  static constexpr int OFF_C = STAGES * STAGE_BYTES;      // fp16 output tile, BN/64 swizzled boxes
+  static constexpr int C_BYTES = EPI ? BM * BN * 2 : 0;
+  static constexpr int OFF_BAR = OFF_C + C_BYTES;
+  static constexpr int SMEM = OFF_BAR + (3 * STAGES + 4) * 8 + 16;   // base is 1024-aligned
   // tensor memory columns
   static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
   static constexpr int SF_BASE = ACC_COLS;
@@ -86,7 +102,7 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 512;
   static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = 192;
+  static constexpr int THREADS = SFST ? 320 : 192;   // + 4 scale warps (warps 6-9)
   static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(BM, BN);
 };
 
@@ -107,14 +123,19 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 
 template <class C, int MAXG>
 __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams<MAXG> P) {
-  extern __shared__ uint8_t smem_raw[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  const uint32_t sbase = raw;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (raw & 1023u) {  // the swizzled tiles need a 1024-aligned base; the launch guarantees it
+    if (threadIdx.x == 0) atomicOr(P.err, kDevErrTimeoutMma);
+    return;
+  }
   const uint32_t bar_full = sbase + C::OFF_BAR;
   const uint32_t bar_empty = bar_full + 8 * C::STAGES;
-  const uint32_t bar_accf = bar_empty + 8 * C::STAGES;
+  const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;      // scales in tensor memory (SFST)
+  const uint32_t bar_accf = bar_sfr + 8 * C::STAGES;
   const uint32_t bar_acce = bar_accf + 8;
   const uint32_t bar_done = bar_acce + 8;
   const uint32_t tmem_slot = bar_done + 8;
@@ -125,6 +146,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
+      mbar_init(bar_sfr + 8 * s, 4);
     }
     mbar_init(bar_accf, 1);
     mbar_init(bar_acce, 4);
@@ -149,7 +171,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
       }
       const uint64_t pol_a = policy_evict_last();   // A tiles are re-read by every N tile
-      const uint64_t pol_b = policy_evict_first();  // B tiles stream (shared only by concurrent CTAs)
+      const uint64_t pol_b = C::POL ? policy_evict_normal() : policy_evict_first();
       uint32_t it = 0;
       for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
@@ -169,6 +191,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           const uint32_t sfb_bytes = (uint32_t)(nbv * nch * 512);
           const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) + nch * 512 +
                                  sfb_bytes * (C::DUAL ? 2 : 1);
+          if (C::DBG & 4) {
+            mbar_arrive(fb);
+            continue;
+          }
           mbar_arrive_expect_tx(fb, bytes);
           tma_load_2d(st, &G.ta, fb, ks * KSTEP_BYTES, mt * BM, pol_a);
           tma_load_2d(st + C::OFF_B, &G.tb, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
@@ -196,13 +222,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         tc::fence_after_sync();
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
-          if (!mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
+          if (!mbar_wait((C::SFST ? bar_sfr : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull))
+            goto done;
           tc::fence_after_sync();
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const int nch = min(4, nk64 - 4 * ks);
           const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
           const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFB_COLS_PER_KB;
-          for (int kk = 0; kk < nch; ++kk) {
+          for (int kk = 0; kk < nch && !(C::DBG & 1) && !C::SFST; ++kk) {
             tc::cp_sf_32x128b_x4(sfa_t + 4 * kk, tc::desc_sf_block(st + C::OFF_SFA + kk * 512));
             for (int nb = 0; nb < C::NB; ++nb) {
               tc::cp_sf_32x128b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
@@ -214,7 +241,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           }
           const uint64_t da = tc::desc_sw128(st), db = tc::desc_sw128(st + C::OFF_B);
           const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
-          for (int kk = 0; kk < nch; ++kk) {
+          for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
             // the k-th 64-element slice starts 32 bytes further (encoded >> 4)
             tc::mma_mxf4nvf4(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk,
@@ -228,6 +255,46 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         tc::commit(bar_accf);
       }
     }
+  } else if (warp >= 6) {
+    // ------------------- scale warps (SFST == 1 only) -------------------
+    // Each warp copies, for its tensor-memory lane quarter, the 16 bytes of
+    // every 512-byte scale block of the stage (row `lane` of the block) into 4
+    // consecutive columns: the same image a 32x128b.warpx4 copy would make.
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    uint32_t it = 0;
+    bool dead = false;
+    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
+      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+      const int nk64 = G.K / 64;
+      const int nks = (nk64 + 3) / 4;
+      for (int ks = 0; ks < nks; ++ks, ++it) {
+        const int s = it % C::STAGES;
+        if (!dead && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) dead = true;
+        if (dead) break;
+        const uint8_t* st = smem_raw + (sbase - raw) + s * C::STAGE_BYTES;
+        const int nch = min(4, nk64 - 4 * ks);
+        const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
+        const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFB_COLS_PER_KB;
+        for (int kk = 0; kk < nch && !(C::DBG & 1); ++kk) {
+          uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
+          tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
+#pragma unroll
+          for (int nb = 0; nb < C::NB; ++nb) {
+            v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB + nb * 2048 + kk * 512 + lane * 16);
+            tc::st_32x32b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
+            if (C::DUAL) {
+              v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB2 + nb * 2048 + kk * 512 + lane * 16);
+              tc::st_32x32b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
+            }
+          }
+        }
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_sfr + 8 * s);
+      }
+      if (dead) break;
+    }
   } else {
     // ---------------------------- epilogue ----------------------------
     const int sub = warp & 3;                 // tensor-memory lane quarter of this warp
@@ -239,10 +306,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       const int mt = local % G.tiles_m, nt = local / G.tiles_m;
       if (!mbar_wait(bar_accf, tile_it & 1, P.err, kDevErrTimeoutMma)) break;
       tc::fence_after_sync();
-      const int row = mt * BM + sub * 32 + lane;
+      const int rloc = sub * 32 + lane;        // row of the tile held by this thread
+      const int row = mt * BM + rloc;
+      if (C::EPI && G.tma_store) {
+        // previous tile's TMA stores must have finished reading the staging tile
+        if (threadIdx.x == 64) bulk_wait_read_all();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+      }
       __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
 #pragma unroll 1
-      for (int cb = 0; cb < C::BN / 32; ++cb) {
+      for (int cb = 0; cb < C::BN / 32 && !(C::DBG & 8); ++cb) {
         uint32_t v[32];
         tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
         uint32_t h[16];
@@ -250,14 +323,34 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           uint32_t u[32];
           tc::ld_32x32b_x32(tmem + lane_base + C::BN + cb * 32, u);
           tc::wait_ld();
+          if (cb == C::BN / 32 - 1) {   // accumulator fully read: let the next tile's MMAs start
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acce);
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j)
             h[j] = pack_h2(silu_mul(__uint_as_float(v[2 * j]), __uint_as_float(u[2 * j])),
                            silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
         } else {
           tc::wait_ld();
+          if (cb == C::BN / 32 - 1) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acce);
+          }
 #pragma unroll
           for (int j = 0; j < 16; ++j) h[j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+        }
+        if (C::EPI && G.tma_store) {
+          // box cb/2 holds 64 columns: row rloc at 128 * rloc, 16-byte chunk q at (q ^ (rloc % 8))
+          uint8_t* box = smem_raw + C::OFF_C + (cb >> 1) * (BM * 128) + rloc * 128;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = ((cb & 1) * 4 + q) ^ (rloc & 7);
+            *reinterpret_cast<uint4*>(box + chunk * 16) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+          }
+          continue;
         }
         const int col0 = nt * C::BN + cb * 32;
         if (row < G.M) {
@@ -271,10 +364,22 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           }
         }
       }
-      tc::fence_before_sync();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_acce);
+      if (C::DBG & 8) {
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_acce);
+      }
+      if (C::EPI && G.tma_store && !(C::DBG & 8)) {
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          for (int b = 0; b < C::BN / 64; ++b)
+            tma_store_2d(&G.tc, sbase + C::OFF_C + b * (BM * 128), nt * C::BN + 64 * b, mt * BM);
+          bulk_commit_group();
+        }
+      }
     }
+    if (threadIdx.x == 64) bulk_wait_all();
   }
 done:
   tc::fence_before_sync();
@@ -331,15 +436,25 @@ int check_out(void* c, int64_t N, int64_t ldc) {
 
 int vec_ok(const void* c, int64_t ldc) { return aligned16(c) && ldc % 8 == 0; }
 
+// Output map for the TMA-store epilogue: fp16 [M, N], 64-column x 128-row boxes
+// with 128-byte swizzle (the staging tile's layout).
+int out_map(CUtensorMap* m, void* c, int64_t M, int64_t N, int64_t ldc) {
+  const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
+  const uint64_t str[1] = {(uint64_t)ldc * 2};
+  const uint32_t box[2] = {64, (uint32_t)BM};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, c, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 }  // namespace
 }  // namespace nvfp4
 
 using namespace nvfp4;
 
-extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa, const void* sfb1,
-                               const void* sfb2, void* c, int64_t M, int64_t N, int64_t K, int64_t lda,
-                               int64_t ldb, int64_t ldc, void* stream) {
-  using C = GemmCfg<128, true, 4>;
+namespace nvfp4 {
+template <class C>
+int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, const void* sfb1,
+             const void* sfb2, void* c, int64_t M, int64_t N, int64_t K, int64_t lda,
+             int64_t ldb, int64_t ldc, void* stream) {
   if (K < 64 || K % 64) return fail(NVFP4_ERR_INVALID, "nvfp4_dual_gemm: K must be a positive multiple of 64");
   int rc;
   if ((rc = check_operand("a", a, sfa, M, K, lda)) || (rc = check_operand("b1", b1, sfb1, N, K, ldb)) ||
@@ -357,6 +472,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   G.c = static_cast<__half*>(c);
   G.ldc = ldc;
   G.vec_ok = vec_ok(c, ldc);
+  G.tma_store = G.vec_ok && out_map(&G.tc, c, M, N, ldc) == NVFP4_OK;
   G.M = (int)M; G.N = (int)N; G.K = (int)K;
   G.tiles_m = (int)((M + BM - 1) / BM);
   G.tiles_n = (int)((N + C::BN - 1) / C::BN);
@@ -368,8 +484,17 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   return launch_gemm<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream) {
-  using C = GemmCfg<256, false, 4>;
+}  // namespace nvfp4
+
+extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa, const void* sfb1,
+                               const void* sfb2, void* c, int64_t M, int64_t N, int64_t K, int64_t lda,
+                               int64_t ldb, int64_t ldc, void* stream) {
+  return dual_run<GemmCfg<128, true, 4, 0, 1, 0, 0>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb, ldc, stream);
+}
+
+namespace nvfp4 {
+template <class C>
+int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
   constexpr int MAXG = 32;
   if (!groups || num_groups < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_grouped_gemm: no groups");
   uint32_t* err = device_error_word();
@@ -397,6 +522,7 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
       G.c = static_cast<__half*>(q.c);
       G.ldc = q.ldc;
       G.vec_ok = vec_ok(q.c, q.ldc);
+      G.tma_store = G.vec_ok && out_map(&G.tc, q.c, q.M, q.N, q.ldc) == NVFP4_OK;
       G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
       G.tiles_m = (int)((q.M + BM - 1) / BM);
       G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
@@ -412,6 +538,11 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
     if (rc) return rc;
   }
   return NVFP4_OK;
+}
+}  // namespace nvfp4
+
+extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream) {
+  return grouped_run<GemmCfg<256, false, 4, 0, 1, 0, 0>>(groups, num_groups, stream);
 }
 
 // ---------------------------------------------------------------------------

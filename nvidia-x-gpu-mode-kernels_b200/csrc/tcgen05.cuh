@@ -95,6 +95,15 @@ __device__ __forceinline__ void ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32])
       : "r"(taddr));
 }
 
+// Each thread writes 4 consecutive 32-bit columns of its own lane
+// (lane 32 * (warp % 4) + thread).
+__device__ __forceinline__ void st_32x32b_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};"
+               :: "r"(taddr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 }  // namespace tc
