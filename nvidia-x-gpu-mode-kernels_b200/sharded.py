@@ -68,3 +68,65 @@ class ShardedGemv:
             lo, hi = row_split(self.M, self.world, r)
             parts.append(self.gathered[r, :, : hi - lo])
         return torch.cat(parts, dim=1).transpose(0, 1).unsqueeze(1)
+
+
+def lpt_assign(costs: list[float], world: int) -> list[int]:
+    """Longest-processing-time-first: each group (largest cost first) goes to
+    the rank with the least assigned cost.  Deterministic on ties (lowest
+    rank, then group index)."""
+    load = [0.0] * world
+    owner = [0] * len(costs)
+    for g in sorted(range(len(costs)), key=lambda i: (-costs[i], i)):
+        r = min(range(world), key=lambda k: (load[k], k))
+        owner[g] = r
+        load[r] += costs[g]
+    return owner
+
+
+class ShardedGroupedGemm:
+    """Grouped GEMM sharded by group across ranks.
+
+    Groups are bin-packed onto ranks by FLOPs (``lpt_assign``); each rank runs
+    one grouped launch over its own groups, writing into a flat fp16 buffer
+    laid out group after group; one all-gather of the buffers (padded to the
+    largest rank's size) lets every rank unpack every group's output.
+    """
+
+    def __init__(self, Ms, N: int, K: int, group=None, device=None):
+        self.Ms, self.N, self.K = list(Ms), N, K
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.owner = lpt_assign([m * N * K for m in self.Ms], self.world)
+        self.mine = [g for g in range(len(self.Ms)) if self.owner[g] == self.rank]
+        sizes = [sum(self.Ms[g] * N for g in range(len(self.Ms)) if self.owner[g] == r) for r in range(self.world)]
+        self.pad = max(max(sizes), 1)
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.local = torch.zeros(self.pad, dtype=torch.float16, device=dev)
+        self.gathered = torch.empty(self.world * self.pad, dtype=torch.float16, device=dev)
+        self.local_views = []
+        off = 0
+        for g in self.mine:
+            self.local_views.append(self.local[off: off + self.Ms[g] * N].view(self.Ms[g], N))
+            off += self.Ms[g] * N
+
+    def __call__(self, grouped_gemm, a_list, b_list, sfa_list, sfb_list):
+        """Lists hold this rank's groups only, in ``self.mine`` order."""
+        if self.mine:
+            grouped_gemm(a_list, b_list, sfa_list, sfb_list, self.local_views)
+        if self.world > 1:
+            dist.all_gather_into_tensor(self.gathered, self.local, group=self.group)
+        else:
+            self.gathered.copy_(self.local)
+        return self.gathered
+
+    def outputs(self):
+        """Every group's [M_g, N] output, viewed from the gathered buffer."""
+        offs = [0] * self.world
+        out = [None] * len(self.Ms)
+        for g, m in enumerate(self.Ms):
+            r = self.owner[g]
+            base = r * self.pad + offs[r]
+            out[g] = self.gathered[base: base + m * self.N].view(m, self.N)
+            offs[r] += m * self.N
+        return out
