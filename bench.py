@@ -320,16 +320,24 @@ def our_arm(args, world, rank, local):
     flush = Flusher()
 
     c_local = sh.local[:, :, : hi - lo].permute(2, 1, 0)
+    fused = pkg.sharded.FusedShardedGemv(M, K, L) if world > 1 else None
 
     def step_split(ev):
-        # one GEMV (+ the output all-gather when world > 1); events split the two
+        # one GEMV; with world > 1 the fused kernel also delivers every rank's rows
+        ev_mark(ev)
+        if fused is None:
+            pkg.custom_kernel(a, b, sfa, sfb, c_local)
+        else:
+            fused(a, b, sfa, sfb)
+        ev_mark(ev)
+
+    def step_nccl(ev):
         ev_mark(ev)
         pkg.custom_kernel(a, b, sfa, sfb, c_local)
         ev_mark(ev)
-        if world > 1:
-            import torch.distributed as dist
-            dist.all_gather_into_tensor(sh.gathered.view(-1), sh.local.view(-1))
-            ev_mark(ev)
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(sh.gathered.view(-1), sh.local.view(-1))
+        ev_mark(ev)
 
     # correctness gate before timing (rank-local rows against a CPU row sample)
     sh(pkg.custom_kernel, a, b, sfa, sfb)
@@ -342,23 +350,34 @@ def our_arm(args, world, rank, local):
         barrier(world)
         t_wall = time.perf_counter() - t_wall0
     step_ms = [sum(s) for s in segs]
-    kern_ms = [s[0] for s in segs]
-    mean_step, mean_kern = max_over_ranks(world, [statistics.mean(step_ms), statistics.mean(kern_ms)])
+    mean_step, = max_over_ranks(world, [statistics.mean(step_ms)])
+    if world > 1:
+        # the same rows through the plain kernel + an NCCL all-gather, for comparison
+        nsegs = time_steps(step_nccl, args.steps, args.warmup, flush)
+        nccl_step, nccl_kern = max_over_ranks(world, [statistics.mean(sum(s) for s in nsegs),
+                                                      statistics.mean(s[0] for s in nsegs)])
+        mean_kern = nccl_kern
+    else:
+        mean_kern = mean_step
     nbytes = full.nbytes_algorithmic()
     value = nbytes / (mean_step * 1e-3) / 1e9
 
     # end to end through the public API from pinned host buffers
     a_p, b_p, sfa_p, sfb_p = (t.permute(2, 0, 1).contiguous().pin_memory() for t in (a_h, b_h, sfa_h, sfb_h))
-    out_host = torch.empty(sh.gathered.shape, dtype=torch.float16).pin_memory()
+    out_src = fused.out_flat if fused is not None else sh.gathered
+    out_host = torch.empty(out_src.shape, dtype=torch.float16).pin_memory()
     a_d, b_d, sfa_d, sfb_d = (torch.empty_like(t, device=dev) for t in (a_p, b_p, sfa_p, sfb_p))
 
     def e2e_step(ev):
         ev_mark(ev)
         for d, h in ((a_d, a_p), (b_d, b_p), (sfa_d, sfa_p), (sfb_d, sfb_p)):
             d.copy_(h, non_blocking=True)
-        sh(pkg.custom_kernel, a_d.permute(1, 2, 0), b_d.permute(1, 2, 0), sfa_d.permute(1, 2, 0),
-           sfb_d.permute(1, 2, 0))
-        out_host.copy_(sh.gathered, non_blocking=True)
+        args4 = (a_d.permute(1, 2, 0), b_d.permute(1, 2, 0), sfa_d.permute(1, 2, 0), sfb_d.permute(1, 2, 0))
+        if fused is not None:
+            fused(*args4)
+        else:
+            sh(pkg.custom_kernel, *args4)
+        out_host.copy_(out_src, non_blocking=True)
         ev_mark(ev)
 
     e2e_ms = [s[0] for s in time_steps(e2e_step, max(3, args.steps // 4), 2, flush)]
@@ -379,7 +398,8 @@ def our_arm(args, world, rank, local):
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e2m1/e4m3 in, f32 acc, f16 out",
         "data": "synthetic (seed 0; codes uniform 0..255, scales 2^u, u in [-3,3])",
         "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1" +
-                   (f", row-sharded x{world} + NCCL all-gather" if world > 1 else ""),
+                   (f", row-sharded x{world}, all-gather fused into the kernel (NVLink peer stores)"
+                    if world > 1 else ""),
                    "M": M, "K": K, "L": L, "l2": "flushed before every step (512 MiB write, then 256 MiB read)",
                    "parallelism": f"rows/{world}" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
@@ -390,6 +410,10 @@ def our_arm(args, world, rank, local):
                 "h2d_bytes_per_step": h2d_all, "d2h_bytes_per_step": d2h_all,
                 "ms_per_step": round(e2e_mean, 4)},
         "gpu_launches": args.steps * 1,
+        "allgather": (None if world == 1 else {
+            "fused_peer_store_us_per_step": round(mean_step * 1e3, 3),
+            "nccl_us_per_step": round(nccl_step * 1e3, 3),
+            "kernel_only_us": round(mean_kern * 1e3, 3)}),
         "clocks": clk.summary(),
         "wall_s_timed_region": round(t_wall, 3),
     }

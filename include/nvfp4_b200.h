@@ -73,6 +73,34 @@ NVFP4_API int nvfp4_gemv(const void* a, const void* b, const void* sfa, const vo
                int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
                int64_t c_sm, int64_t c_sl, void* stream);
 
+/* Number of CTAs the nvfp4_gemv TMA path launches for this shape (aligned inputs). */
+NVFP4_API int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid);
+
+/*
+ * Row-sharded GEMV with the output all-gather fused in (one launch per rank,
+ * one rank per GPU).  This rank computes rows [m_off, m_off + M_local) of the
+ * full output (its a / sfa hold only those rows) and stores each result row
+ * into EVERY rank's full-size output buffer peer_out[r] (device pointers valid
+ * on this GPU: peer memory over NVLink, e.g. from torch symmetric memory), with
+ * element strides c_sm / c_sl.  Each CTA then adds 1 to every rank's 32-bit
+ * counter peer_flags[r] (system-scope atomics after a system fence), and the
+ * launch ends only when this rank's counter has reached `target`: the caller
+ * keeps target as the running total of sum-over-ranks nvfp4_gemv_grid() of
+ * every call so far (counters start at 0 and are never reset).  The wait is
+ * bounded (2 s, error bit 4 in nvfp4_device_errors()).  All ranks must make
+ * the same sequence of calls.  Requires the aligned (TMA) path; world <= 8.
+ * Replaces "nvfp4_gemv_forward + NCCL all-gather" (the reference has no
+ * distributed code; the north star asks for row sharding with an output
+ * all-gather).
+ */
+NVFP4_API int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
+                                   int64_t M_local, int64_t K, int64_t L,
+                                   int64_t a_sm, int64_t a_sl, int64_t b_sl,
+                                   int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
+                                   void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
+                                   uint32_t* const* peer_flags, int world, int rank, uint32_t target,
+                                   void* stream);
+
 /*
  * Reads this device's error word (bits set by device-side bounded waits that
  * expired) and, when `clear` is non-zero, resets it.  Synchronises the device.

@@ -35,6 +35,10 @@ SIGNATURES: dict[str, list] = {
     "nvfp4_dual_gemm": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_grouped_gemm": [ctypes.POINTER(Group), ctypes.c_int, VP],
     "nvfp4_mma_peak": [ctypes.c_int, VP],
+    "nvfp4_gemv_grid": [I64, I64, I64, ctypes.POINTER(I64)],
+    "nvfp4_gemv_allgather": [VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, I64, I64, I64,
+                             ctypes.POINTER(VP), I64, I64, I64, ctypes.POINTER(VP), ctypes.c_int, ctypes.c_int,
+                             ctypes.c_uint32, VP],
 }
 
 STATUS_NAMES = {0: "OK", 1: "INVALID", 2: "ALIGNMENT", 3: "CUDA", 4: "TIMEOUT", 5: "UNSUPPORTED"}

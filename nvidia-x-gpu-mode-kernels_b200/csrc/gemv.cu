@@ -42,6 +42,8 @@
 namespace nvfp4 {
 namespace {
 
+constexpr int kMaxRanks = 8;
+
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 struct GemvArgs {
@@ -53,6 +55,14 @@ struct GemvArgs {
   int64_t M, K, L;
   int64_t a_sm, a_sl, b_sl, sfa_sm, sfa_sl, sfb_sl, c_sm, c_sl;
   uint32_t* err;
+  // Fused all-gather (world > 0): rows also go to every rank's output at row
+  // offset m_off, then every CTA adds one arrival to every rank's flag.
+  __half* peer_c[kMaxRanks];
+  uint32_t* peer_flag[kMaxRanks];
+  int world;
+  int rank;
+  int64_t m_off;
+  uint32_t target;   // cumulative arrivals this rank's flag must reach
 };
 
 struct GemvMaps {
@@ -240,7 +250,38 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
       float v = 0.f;
 #pragma unroll
       for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
-      if (m0 + row < M) p.c[l * p.c_sl + (m0 + row) * p.c_sm] = __float2half_rn(v);
+      if (m0 + row < M) {
+        const __half hv = __float2half_rn(v);
+        if (p.world == 0) {
+          p.c[l * p.c_sl + (m0 + row) * p.c_sm] = hv;
+        } else {
+          const int64_t off = l * p.c_sl + (p.m_off + m0 + row) * p.c_sm;
+          for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
+        }
+      }
+    }
+  }
+  if (p.world > 0) {
+    // every consumer thread's stores are issued; publish them, then count in
+    asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      for (int r = 0; r < p.world; ++r) atomicAdd_system(p.peer_flag[r], 1u);
+      if (blockIdx.x == 0) {
+        // the launch completes only once every rank's rows have arrived here
+        const uint32_t* f = p.peer_flag[p.rank];
+        const uint64_t t0 = globaltimer();
+        for (uint32_t it = 0;; ++it) {
+          uint32_t v;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+          if ((int32_t)(v - p.target) >= 0) break;
+          if ((it & 63u) == 63u && globaltimer() - t0 > kWaitBudgetNs) {
+            atomicOr(p.err, kDevErrTimeoutPeer);
+            break;
+          }
+        }
+        __threadfence_system();
+      }
     }
   }
 }
@@ -371,7 +412,18 @@ int cached_maps(const GemvArgs& p, GemvMaps& out) {
 }
 
 template <class C>
-int launch_tma(const GemvArgs& p, cudaStream_t stream) {
+int64_t grid_of(const GemvArgs& p) {
+  const int64_t ntiles = (p.M + C::ROWS - 1) / C::ROWS * p.L;
+  int64_t grid = (int64_t)sm_count() * C::MINB;
+  return ntiles < grid ? ntiles : grid;
+}
+
+template <class C>
+int launch_tma(const GemvArgs& p, cudaStream_t stream, int64_t* grid_out) {
+  if (grid_out) {
+    *grid_out = grid_of<C>(p);
+    return NVFP4_OK;
+  }
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -383,9 +435,7 @@ int launch_tma(const GemvArgs& p, cudaStream_t stream) {
   GemvMaps maps;
   int rc = cached_maps<C>(p, maps);
   if (rc) return rc;
-  const int64_t ntiles = (p.M + C::ROWS - 1) / C::ROWS * p.L;
-  int64_t grid = (int64_t)sm_count() * C::MINB;
-  if (ntiles < grid) grid = ntiles;
+  const int64_t grid = grid_of<C>(p);
   gemv_tma_kernel<C><<<(unsigned)grid, C::THREADS, C::SMEM, stream>>>(maps, p);
   return check_launch("gemv_tma_kernel");
 }
@@ -402,17 +452,18 @@ int launch_generic(const GemvArgs& p, cudaStream_t stream) {
 // Configuration by shape: the row slice per stage matches K (one 2 KB box row
 // when K allows), and small problems use short tiles so that every SM gets
 // work.
-int gemv_dispatch(const GemvArgs& p, cudaStream_t st) {
+// With grid_out set, only reports the grid the launch would use.
+int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullptr) {
   const int64_t kb = p.K / 2;
   const int64_t rows = p.M * p.L;
   const int64_t sms = sm_count();
   if (rows < sms * 16) {
-    if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st);
-    return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st);
+    if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
+    return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
   }
-  if (kb >= 2048) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st);
-  if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st);
-  return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st);
+  if (kb >= 2048) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
+  if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
+  return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st, grid_out);
 }
 
 }  // namespace nvfp4
@@ -429,10 +480,17 @@ extern "C" int nvfp4_gemv(const void* a, const void* b, const void* sfa, const v
   if (a_sm < K / 2 || sfa_sm < K / 16 || (L > 1 && (a_sl <= 0 || b_sl <= 0 || sfa_sl <= 0 || sfb_sl <= 0)) ||
       c_sm == 0 || (L > 1 && c_sl == 0))
     return fail(NVFP4_ERR_INVALID, "nvfp4_gemv: invalid strides");
-  GemvArgs args{static_cast<const uint8_t*>(a), static_cast<const uint8_t*>(b),
-                static_cast<const uint8_t*>(sfa), static_cast<const uint8_t*>(sfb),
-                static_cast<__half*>(c), M, K, L, a_sm, a_sl, b_sl, sfa_sm, sfa_sl, sfb_sl, c_sm, c_sl,
-                device_error_word()};
+  GemvArgs args{};
+  args.a = static_cast<const uint8_t*>(a);
+  args.b = static_cast<const uint8_t*>(b);
+  args.sfa = static_cast<const uint8_t*>(sfa);
+  args.sfb = static_cast<const uint8_t*>(sfb);
+  args.c = static_cast<__half*>(c);
+  args.M = M; args.K = K; args.L = L;
+  args.a_sm = a_sm; args.a_sl = a_sl; args.b_sl = b_sl;
+  args.sfa_sm = sfa_sm; args.sfa_sl = sfa_sl; args.sfb_sl = sfb_sl;
+  args.c_sm = c_sm; args.c_sl = c_sl;
+  args.err = device_error_word();
   if (!args.err) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv: cannot resolve the device error word");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool tma_ok = aligned16(a) && aligned16(b) && aligned16(sfa) && aligned16(sfb) && a_sm % 16 == 0 &&
@@ -440,4 +498,53 @@ extern "C" int nvfp4_gemv(const void* a, const void* b, const void* sfa, const v
                       (L == 1 || (a_sl % 16 == 0 && b_sl % 16 == 0 && sfa_sl % 16 == 0 && sfb_sl % 16 == 0));
   if (!tma_ok) return launch_generic(args, st);
   return gemv_dispatch(args, st);
+}
+
+extern "C" int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid) {
+  using namespace nvfp4;
+  if (!grid || M < 1 || L < 1 || K < 16 || K % 16) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_grid: bad shape");
+  GemvArgs args{};
+  args.M = M; args.K = K; args.L = L;
+  return gemv_dispatch(args, nullptr, grid);
+}
+
+extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
+                                    int64_t M_local, int64_t K, int64_t L, int64_t a_sm, int64_t a_sl,
+                                    int64_t b_sl, int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
+                                    void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
+                                    uint32_t* const* peer_flags, int world, int rank, uint32_t target,
+                                    void* stream) {
+  using namespace nvfp4;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_flags)
+    return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: need 1 <= world <= %d and 0 <= rank < world", kMaxRanks);
+  for (int r = 0; r < world; ++r)
+    if (!peer_out[r] || !peer_flags[r]) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: null peer pointer");
+  if (!a || !b || !sfa || !sfb) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: null input");
+  if (M_local < 1 || L < 1 || K < 16 || K % 16 || m_off < 0 || c_sm == 0 || (L > 1 && c_sl == 0))
+    return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: bad shape or strides");
+  const bool tma_ok = aligned16(a) && aligned16(b) && aligned16(sfa) && aligned16(sfb) && a_sm % 16 == 0 &&
+                      sfa_sm % 16 == 0 &&
+                      (L == 1 || (a_sl % 16 == 0 && b_sl % 16 == 0 && sfa_sl % 16 == 0 && sfb_sl % 16 == 0));
+  if (!tma_ok) return fail(NVFP4_ERR_ALIGNMENT, "nvfp4_gemv_allgather: needs 16-byte aligned pointers and strides");
+  GemvArgs args{};
+  args.a = static_cast<const uint8_t*>(a);
+  args.b = static_cast<const uint8_t*>(b);
+  args.sfa = static_cast<const uint8_t*>(sfa);
+  args.sfb = static_cast<const uint8_t*>(sfb);
+  args.c = static_cast<__half*>(peer_out[rank]);
+  args.M = M_local; args.K = K; args.L = L;
+  args.a_sm = a_sm; args.a_sl = a_sl; args.b_sl = b_sl;
+  args.sfa_sm = sfa_sm; args.sfa_sl = sfa_sl; args.sfb_sl = sfb_sl;
+  args.c_sm = c_sm; args.c_sl = c_sl;
+  args.err = device_error_word();
+  if (!args.err) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv_allgather: cannot resolve the device error word");
+  for (int r = 0; r < world; ++r) {
+    args.peer_c[r] = static_cast<__half*>(peer_out[r]);
+    args.peer_flag[r] = peer_flags[r];
+  }
+  args.world = world;
+  args.rank = rank;
+  args.m_off = m_off;
+  args.target = target;
+  return gemv_dispatch(args, static_cast<cudaStream_t>(stream));
 }

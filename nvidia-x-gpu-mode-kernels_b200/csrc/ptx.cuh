@@ -13,6 +13,7 @@ enum : uint32_t {
   kDevErrTimeoutEmpty = 1u << 1,   // producer gave up waiting for a stage to drain
   kDevErrTimeoutMma   = 1u << 2,   // MMA / epilogue handshake gave up
   kDevErrTimeoutTest  = 1u << 3,   // deliberately unsatisfied wait (self-test)
+  kDevErrTimeoutPeer  = 1u << 4,   // a peer GPU's rows did not arrive (fused all-gather)
 };
 
 // Wait budget for every spin in this library: 2 s of %globaltimer.  A healthy

@@ -130,3 +130,62 @@ class ShardedGroupedGemm:
             out[g] = self.gathered[base: base + m * self.N].view(m, self.N)
             offs[r] += m * self.N
         return out
+
+
+class FusedShardedGemv:
+    """Row-sharded GEMV whose output all-gather is fused into the kernel.
+
+    Every rank owns a full-size output buffer [M, 1, L] (stored L-major, rows
+    contiguous) and a counter word, both in torch symmetric memory so every
+    GPU holds device pointers to every rank's copy.  One launch per call per
+    rank computes this rank's rows and stores them straight into all ranks'
+    buffers over NVLink (``nvfp4_gemv_allgather``); the launch returns once all
+    ranks' rows have landed locally.  No NCCL call on the data path.
+    """
+
+    def __init__(self, M: int, K: int, L: int, group=None, device=None):
+        import ctypes
+        import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        self.M, self.K, self.L = M, K, L
+        self.group = group or dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        if self.world > 8:
+            raise ValueError("FusedShardedGemv supports up to 8 ranks")
+        self.lo, self.hi = row_split(M, self.world, self.rank)
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.out_flat = symm.empty(L * M, dtype=torch.float16, device=dev)
+        self.flags = symm.empty(64, dtype=torch.int32, device=dev)
+        self.flags.zero_()
+        torch.cuda.synchronize(dev)
+        gname = self.group.group_name
+        self._h_out = symm.rendezvous(self.out_flat, gname)
+        self._h_flag = symm.rendezvous(self.flags, gname)
+        self._peer_out = (ctypes.c_void_p * self.world)(*self._h_out.buffer_ptrs)
+        self._peer_flag = (ctypes.c_void_p * self.world)(*self._h_flag.buffer_ptrs)
+        lib = _lib.lib()
+        total = 0
+        for r in range(self.world):
+            lo, hi = row_split(M, self.world, r)
+            g = ctypes.c_int64(0)
+            _lib.check(lib.nvfp4_gemv_grid(hi - lo, K, L, ctypes.byref(g)))
+            total += g.value
+        self.arrivals_per_call = total
+        self.target = 0
+        dist.barrier(self.group)
+
+    def out(self) -> torch.Tensor:
+        """[M, 1, L] view of this rank's copy of the full output."""
+        return self.out_flat.view(self.L, 1, self.M).permute(2, 1, 0)
+
+    def __call__(self, a_rows, b, sfa_rows, sfb) -> torch.Tensor:
+        from . import _lib
+        self.target = (self.target + self.arrivals_per_call) & 0xFFFFFFFF
+        sa, sb, ssa, ssb = a_rows.stride(), b.stride(), sfa_rows.stride(), sfb.stride()
+        _lib.check(_lib.lib().nvfp4_gemv_allgather(
+            a_rows.data_ptr(), b.data_ptr(), sfa_rows.data_ptr(), sfb.data_ptr(),
+            self.hi - self.lo, self.K, self.L, sa[0], sa[2], sb[2], ssa[0], ssa[2], ssb[2],
+            self._peer_out, 1, self.M, self.lo, self._peer_flag, self.world, self.rank, self.target,
+            torch.cuda.current_stream().cuda_stream))
+        return self.out()
