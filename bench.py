@@ -167,7 +167,7 @@ class Flusher:
         torch.sum(self.rbuf, dim=0, out=self.out)
 
 
-def time_steps(step, steps, warmup, flush, marks=1):
+def time_steps(step, steps, warmup, flush, marks=1, align=None):
     """Runs `warmup` untimed steps, then `steps` timed ones.  `step(ev)` records
     its own events into the list `ev` (first and last bracket the step; extra
     events split it).  Returns per-step lists of segment durations in ms."""
@@ -177,6 +177,8 @@ def time_steps(step, steps, warmup, flush, marks=1):
     recs = []
     for _ in range(steps):
         flush()
+        if align is not None:
+            align()          # line the ranks' streams up (outside the timed events)
         ev = []
         step(ev)
         recs.append(ev)
@@ -321,6 +323,11 @@ def our_arm(args, world, rank, local):
 
     c_local = sh.local[:, :, : hi - lo].permute(2, 1, 0)
     fused = pkg.sharded.FusedShardedGemv(M, K, L) if world > 1 else None
+    align = None
+    if world > 1:
+        import torch.distributed as dist
+        one = torch.zeros(1, device=dev)
+        align = lambda: dist.all_reduce(one)
 
     def step_split(ev):
         # one GEMV; with world > 1 the fused kernel also delivers every rank's rows
@@ -346,14 +353,14 @@ def our_arm(args, world, rank, local):
     barrier(world)
     with ClockSampler(local) as clk:
         t_wall0 = time.perf_counter()
-        segs = time_steps(step_split, args.steps, args.warmup, flush)
+        segs = time_steps(step_split, args.steps, args.warmup, flush, align=align)
         barrier(world)
         t_wall = time.perf_counter() - t_wall0
     step_ms = [sum(s) for s in segs]
     mean_step, = max_over_ranks(world, [statistics.mean(step_ms)])
     if world > 1:
         # the same rows through the plain kernel + an NCCL all-gather, for comparison
-        nsegs = time_steps(step_nccl, args.steps, args.warmup, flush)
+        nsegs = time_steps(step_nccl, args.steps, args.warmup, flush, align=align)
         nccl_step, nccl_kern = max_over_ranks(world, [statistics.mean(sum(s) for s in nsegs),
                                                       statistics.mean(s[0] for s in nsegs)])
         mean_kern = nccl_kern
@@ -400,7 +407,9 @@ def our_arm(args, world, rank, local):
         "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1" +
                    (f", row-sharded x{world}, all-gather fused into the kernel (NVLink peer stores)"
                     if world > 1 else ""),
-                   "M": M, "K": K, "L": L, "l2": "flushed before every step (512 MiB write, then 256 MiB read)",
+                   "M": M, "K": K, "L": L, "l2": "flushed before every step (512 MiB write, then 256 MiB read)" +
+                   ("; ranks aligned by a 1-element all-reduce before each step, outside the timed events"
+                    if world > 1 else ""),
                    "parallelism": f"rows/{world}" if world > 1 else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk_kind,
