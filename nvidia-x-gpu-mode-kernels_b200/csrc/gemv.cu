@@ -63,6 +63,7 @@ struct GemvArgs {
   int rank;
   int64_t m_off;
   uint32_t target;   // cumulative arrivals this rank's flag must reach
+  int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no arrivals
 };
 
 struct GemvMaps {
@@ -256,7 +257,8 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
           p.c[l * p.c_sl + (m0 + row) * p.c_sm] = hv;
         } else {
           const int64_t off = l * p.c_sl + (p.m_off + m0 + row) * p.c_sm;
-          for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
+          if (p.dbg & 1) p.c[off] = hv;
+          else for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
         }
       }
     }
@@ -266,8 +268,9 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
     if (threadIdx.x == 0) {
       __threadfence_system();
-      for (int r = 0; r < p.world; ++r) atomicAdd_system(p.peer_flag[r], 1u);
-      if (blockIdx.x == 0) {
+      if (!(p.dbg & 4))
+        for (int r = 0; r < p.world; ++r) atomicAdd_system(p.peer_flag[r], 1u);
+      if (blockIdx.x == 0 && !(p.dbg & 2)) {
         // the launch completes only once every rank's rows have arrived here
         const uint32_t* f = p.peer_flag[p.rank];
         const uint64_t t0 = globaltimer();
@@ -508,6 +511,8 @@ extern "C" int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid) {
   return gemv_dispatch(args, nullptr, grid);
 }
 
+static int g_gather_dbg = 0;   // set only by tuning probes that compile this file in
+
 extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
                                     int64_t M_local, int64_t K, int64_t L, int64_t a_sm, int64_t a_sl,
                                     int64_t b_sl, int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
@@ -546,5 +551,6 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
   args.rank = rank;
   args.m_off = m_off;
   args.target = target;
+  args.dbg = g_gather_dbg;
   return gemv_dispatch(args, static_cast<cudaStream_t>(stream));
 }
