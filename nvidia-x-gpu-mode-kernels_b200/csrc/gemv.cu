@@ -269,7 +269,8 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     if (threadIdx.x == 0) {
       __threadfence_system();
       if (!(p.dbg & 4))
-        for (int r = 0; r < p.world; ++r) atomicAdd_system(p.peer_flag[r], 1u);
+        for (int r = 0; r < p.world; ++r)   // no-return reductions: no round trip per peer
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" :: "l"(p.peer_flag[r]) : "memory");
       if (blockIdx.x == 0 && !(p.dbg & 2)) {
         // the launch completes only once every rank's rows have arrived here
         const uint32_t* f = p.peer_flag[p.rank];
