@@ -82,23 +82,24 @@ NVFP4_API int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid);
  * full output (its a / sfa hold only those rows) and stores each result row
  * into EVERY rank's full-size output buffer peer_out[r] (device pointers valid
  * on this GPU: peer memory over NVLink, e.g. from torch symmetric memory), with
- * element strides c_sm / c_sl.  Each CTA then adds 1 to every rank's 32-bit
- * counter peer_flags[r] (system-scope atomics after a system fence), and the
- * launch ends only when this rank's counter has reached `target`: the caller
- * keeps target as the running total of sum-over-ranks nvfp4_gemv_grid() of
- * every call so far (counters start at 0 and are never reset).  The wait is
- * bounded (2 s, error bit 4 in nvfp4_device_errors()).  All ranks must make
- * the same sequence of calls.  Requires the aligned (TMA) path; world <= 8.
- * Replaces "nvfp4_gemv_forward + NCCL all-gather" (the reference has no
- * distributed code; the north star asks for row sharding with an output
- * all-gather).
+ * element strides c_sm / c_sl.  peer_flags[r] is rank r's flag buffer: at least
+ * 32 zero-initialised 32-bit words in memory every rank can reach.  Word 16 of
+ * this rank's buffer counts its finished CTAs; the last CTA writes `epoch` into
+ * word `rank` of every rank's buffer and waits until this rank's words 0..world-1
+ * all hold `epoch`, so the launch ends with every rank's rows present locally.
+ * `epoch` is the 1-based count of calls made with these flag buffers (the same
+ * on every rank; the shape must stay the same between calls).  The wait is
+ * bounded (2 s, error bit 4 in nvfp4_device_errors()).  Requires the aligned
+ * (TMA) path; world <= 8.  Replaces "nvfp4_gemv_forward + an output
+ * all-gather" (the reference has no distributed code; the north star asks for
+ * row sharding with an output all-gather).
  */
 NVFP4_API int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
                                    int64_t M_local, int64_t K, int64_t L,
                                    int64_t a_sm, int64_t a_sl, int64_t b_sl,
                                    int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
                                    void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
-                                   uint32_t* const* peer_flags, int world, int rank, uint32_t target,
+                                   uint32_t* const* peer_flags, int world, int rank, uint32_t epoch,
                                    void* stream);
 
 /*

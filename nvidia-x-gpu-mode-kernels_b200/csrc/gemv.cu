@@ -43,6 +43,7 @@ namespace nvfp4 {
 namespace {
 
 constexpr int kMaxRanks = 8;
+constexpr int kCtaCounter = 16;   // flag-buffer word counting this rank's finished CTAs
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -62,8 +63,8 @@ struct GemvArgs {
   int world;
   int rank;
   int64_t m_off;
-  uint32_t target;   // cumulative arrivals this rank's flag must reach
-  int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no arrivals
+  uint32_t epoch;    // 1-based call count of this gather (same on every rank)
+  int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no epoch stores
 };
 
 struct GemvMaps {
@@ -264,24 +265,33 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     }
   }
   if (p.world > 0) {
-    // every consumer thread's stores are issued; publish them, then count in
+    // Completion, two levels.  Each CTA counts itself into this rank's local
+    // counter (word kCtaCounter of its flag buffer); the CTA that completes the
+    // count is last on this GPU, so every row of this rank has been stored: it
+    // publishes them (system fence) and writes the call's epoch into word
+    // `rank` of every rank's flag buffer, then waits until every rank's word
+    // holds this epoch, i.e. all rows of all ranks have landed here.
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
     if (threadIdx.x == 0) {
-      __threadfence_system();
-      if (!(p.dbg & 4))
-        for (int r = 0; r < p.world; ++r)   // no-return reductions: no round trip per peer
-          asm volatile("red.release.sys.global.add.u32 [%0], 1;" :: "l"(p.peer_flag[r]) : "memory");
-      if (blockIdx.x == 0 && !(p.dbg & 2)) {
-        // the launch completes only once every rank's rows have arrived here
-        const uint32_t* f = p.peer_flag[p.rank];
+      __threadfence();
+      uint32_t* mine = p.peer_flag[p.rank];
+      const uint32_t done = atomicAdd(mine + kCtaCounter, 1u) + 1u;
+      if (done == p.epoch * gridDim.x) {
+        __threadfence_system();
+        if (!(p.dbg & 4))
+          for (int r = 0; r < p.world; ++r)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(p.epoch)
+                         : "memory");
         const uint64_t t0 = globaltimer();
-        for (uint32_t it = 0;; ++it) {
-          uint32_t v;
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-          if ((int32_t)(v - p.target) >= 0) break;
-          if ((it & 63u) == 63u && globaltimer() - t0 > kWaitBudgetNs) {
-            atomicOr(p.err, kDevErrTimeoutPeer);
-            break;
+        for (int r = 0; r < p.world && !(p.dbg & 2); ++r) {
+          for (uint32_t it = 0;; ++it) {
+            uint32_t v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
+            if ((int32_t)(v - p.epoch) >= 0) break;
+            if ((it & 63u) == 63u && globaltimer() - t0 > kWaitBudgetNs) {
+              atomicOr(p.err, kDevErrTimeoutPeer);
+              break;
+            }
           }
         }
         __threadfence_system();
@@ -518,9 +528,10 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
                                     int64_t M_local, int64_t K, int64_t L, int64_t a_sm, int64_t a_sl,
                                     int64_t b_sl, int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
                                     void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
-                                    uint32_t* const* peer_flags, int world, int rank, uint32_t target,
+                                    uint32_t* const* peer_flags, int world, int rank, uint32_t epoch,
                                     void* stream) {
   using namespace nvfp4;
+  if (epoch == 0) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: epoch counts calls from 1");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_flags)
     return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: need 1 <= world <= %d and 0 <= rank < world", kMaxRanks);
   for (int r = 0; r < world; ++r)
@@ -551,7 +562,7 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
   args.world = world;
   args.rank = rank;
   args.m_off = m_off;
-  args.target = target;
+  args.epoch = epoch;
   args.dbg = g_gather_dbg;
   return gemv_dispatch(args, static_cast<cudaStream_t>(stream));
 }

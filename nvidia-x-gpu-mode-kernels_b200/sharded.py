@@ -140,7 +140,9 @@ class FusedShardedGemv:
     GPU holds device pointers to every rank's copy.  One launch per call per
     rank computes this rank's rows and stores them straight into all ranks'
     buffers over NVLink (``nvfp4_gemv_allgather``); the launch returns once all
-    ranks' rows have landed locally.  No NCCL call on the data path.
+    ranks' rows have landed locally.  No NCCL call on the data path.  The flag
+    words (per-source-rank epochs and a CTA counter) are reused across calls
+    with a running epoch, so one instance serves one fixed shape.
     """
 
     def __init__(self, M: int, K: int, L: int, group=None, device=None):
@@ -164,15 +166,7 @@ class FusedShardedGemv:
         self._h_flag = symm.rendezvous(self.flags, gname)
         self._peer_out = (ctypes.c_void_p * self.world)(*self._h_out.buffer_ptrs)
         self._peer_flag = (ctypes.c_void_p * self.world)(*self._h_flag.buffer_ptrs)
-        lib = _lib.lib()
-        total = 0
-        for r in range(self.world):
-            lo, hi = row_split(M, self.world, r)
-            g = ctypes.c_int64(0)
-            _lib.check(lib.nvfp4_gemv_grid(hi - lo, K, L, ctypes.byref(g)))
-            total += g.value
-        self.arrivals_per_call = total
-        self.target = 0
+        self.epoch = 0
         dist.barrier(self.group)
 
     def out(self) -> torch.Tensor:
@@ -181,11 +175,11 @@ class FusedShardedGemv:
 
     def __call__(self, a_rows, b, sfa_rows, sfb) -> torch.Tensor:
         from . import _lib
-        self.target = (self.target + self.arrivals_per_call) & 0xFFFFFFFF
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
         sa, sb, ssa, ssb = a_rows.stride(), b.stride(), sfa_rows.stride(), sfb.stride()
         _lib.check(_lib.lib().nvfp4_gemv_allgather(
             a_rows.data_ptr(), b.data_ptr(), sfa_rows.data_ptr(), sfb.data_ptr(),
             self.hi - self.lo, self.K, self.L, sa[0], sa[2], sb[2], ssa[0], ssa[2], ssb[2],
-            self._peer_out, 1, self.M, self.lo, self._peer_flag, self.world, self.rank, self.target,
+            self._peer_out, 1, self.M, self.lo, self._peer_flag, self.world, self.rank, self.epoch,
             torch.cuda.current_stream().cuda_stream))
         return self.out()
