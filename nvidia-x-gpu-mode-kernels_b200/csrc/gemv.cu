@@ -64,6 +64,7 @@ struct GemvArgs {
   int rank;
   int64_t m_off;
   uint32_t epoch;    // 1-based call count of this gather (same on every rank)
+  int vec_rows;      // c_sm == 1 and 16-byte aligned row runs: whole-piece peer stores
   int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no epoch stores
 };
 
@@ -93,7 +94,8 @@ struct GemvCfg {
   static constexpr int STAGE_BYTES = ((OFF_SFB + SFK) + 127) / 128 * 128;
   static constexpr uint32_t TX = ROWS * KTB + ROWS * SFK + KTB + SFK;
   static constexpr int OFF_RED = STAGES * STAGE_BYTES;                  // float [2][ROWS][NCH]
-  static constexpr int OFF_BAR = OFF_RED + 2 * ROWS * NCH * 4;
+  static constexpr int OFF_HB = OFF_RED + 2 * ROWS * NCH * 4;          // __half [2][ROWS] (fused gather)
+  static constexpr int OFF_BAR = (OFF_HB + 2 * ROWS * 2 + 15) / 16 * 16;
   static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 128;           // + alignment slack
   static_assert(KTB % 512 == 0 && KTB <= 2048, "KTB: 512-byte chunks, box row <= 256 u64");
   static_assert(CW % NCH == 0 && ROWS % GROUPS == 0, "warps must tile (rows x chunks)");
@@ -248,11 +250,17 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
       if (lane == 0) rb[(group * C::RPW + j) * C::NCH + chunk] = v;
     }
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
+    // fused gather with contiguous output rows: stage the tile's results and
+    // send each peer whole 16-byte pieces instead of one 2-byte store per row
+    const bool vec = (C::ROWS % 8 == 0) && p.world > 0 && !(p.dbg & 1) && p.vec_rows && m0 + C::ROWS <= M;
+    __half* hb = reinterpret_cast<__half*>(smem + C::OFF_HB) + parity * C::ROWS;
     for (int row = threadIdx.x; row < C::ROWS; row += C::CW * 32) {
       float v = 0.f;
 #pragma unroll
       for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
-      if (m0 + row < M) {
+      if (vec) {
+        hb[row] = __float2half_rn(v);
+      } else if (m0 + row < M) {
         const __half hv = __float2half_rn(v);
         if (p.world == 0) {
           p.c[l * p.c_sl + (m0 + row) * p.c_sm] = hv;
@@ -261,6 +269,16 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
           if (p.dbg & 1) p.c[off] = hv;
           else for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
         }
+      }
+    }
+    if (vec) {
+      asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
+      constexpr int PIECES = C::ROWS / 8 > 0 ? C::ROWS / 8 : 1;
+      const int t = threadIdx.x;
+      if (t < p.world * PIECES) {
+        const int r = t / PIECES, q = t % PIECES;
+        const uint4 v = *reinterpret_cast<const uint4*>(hb + 8 * q);
+        *reinterpret_cast<uint4*>(p.peer_c[r] + l * p.c_sl + p.m_off + m0 + 8 * q) = v;   // NVLink peer store
       }
     }
   }
@@ -563,6 +581,9 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
   args.rank = rank;
   args.m_off = m_off;
   args.epoch = epoch;
+  bool vec = c_sm == 1 && m_off % 8 == 0 && (L == 1 || c_sl % 8 == 0);
+  for (int r = 0; r < world; ++r) vec = vec && aligned16(peer_out[r]);
+  args.vec_rows = vec ? 1 : 0;
   args.dbg = g_gather_dbg;
   return gemv_dispatch(args, static_cast<cudaStream_t>(stream));
 }
