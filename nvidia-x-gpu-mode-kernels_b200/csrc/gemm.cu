@@ -103,6 +103,9 @@ struct GemmCfg {
   static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
   static_assert(SMEM <= 232448, "shared memory budget");
   static constexpr int THREADS = SFST ? 320 : 192;   // + 4 scale warps (warps 6-9)
+  static constexpr bool PAIR = false;
+  static constexpr int TILE_M = BM;
+  static constexpr int B_BOX = BN;
   static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(BM, BN);
 };
 
@@ -390,6 +393,293 @@ done:
   }
 }
 
+// ===========================================================================
+// CTA-pair variant (tcgen05.mma.cta_group::2).  A cluster of two CTAs on two
+// SMs computes a 256 x BN tile: each CTA holds 128 rows of A and BN/2 rows of
+// each B operand in its shared memory and the 128 x BN accumulator of its own
+// rows in its tensor memory; the leader CTA (cluster rank 0) issues every MMA.
+// Against the single-CTA kernel each CTA streams a third fewer bytes per FLOP
+// (B is split across the pair instead of loaded by both), which is what the
+// single-CTA kernel is limited by (shared-memory fill bandwidth per SM).
+//   * operand TMA loads use the .cta_group::2 form and complete on the
+//     leader's `full` barrier (no multicast anywhere);
+//   * scale blocks go to this CTA's shared memory (local `sf_full` barrier);
+//     four scale warps per CTA write them into this CTA's tensor memory: A
+//     scales as in the single-CTA kernel, B scales in the pair layout (scale
+//     rows [0, BN/2) in lane quarters 0-1, rows [BN/2, BN) in quarters 2-3,
+//     column j holding rows 32j..32j+31 of the half), then arrive on the
+//     leader's `sf_ready` barrier across the cluster;
+//   * the leader commits each stage to both CTAs' `empty` barriers and each
+//     finished accumulator to both CTAs' `accf`; both CTAs' epilogue warps
+//     arrive on the leader's `acce`.
+// ===========================================================================
+template <int BN_, bool DUAL_, int STAGES_>
+struct Gemm2Cfg {
+  static constexpr int BN = BN_;                           // N per pair MMA (per B operand)
+  static constexpr bool DUAL = DUAL_;
+  static constexpr int STAGES = STAGES_;
+  static constexpr int HB = BN / 2;                        // B rows per CTA
+  static constexpr int NB = (BN + 127) / 128;              // 128-row scale blocks of B per tile
+  static constexpr int A_BYTES = BM * KSTEP_BYTES;
+  static constexpr int B_BYTES = HB * KSTEP_BYTES;
+  static constexpr int OFF_B = A_BYTES;
+  static constexpr int OFF_B2 = OFF_B + B_BYTES;
+  static constexpr int OFF_SFA = OFF_B2 + (DUAL ? B_BYTES : 0);
+  static constexpr int OFF_SFB = OFF_SFA + 2048;
+  static constexpr int SFB_BYTES = NB * 2048;
+  static constexpr int OFF_SFB2 = OFF_SFB + SFB_BYTES;
+  static constexpr int STAGE_BYTES = ((OFF_SFB2 + (DUAL ? SFB_BYTES : 0)) + 1023) / 1024 * 1024;
+  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
+  static constexpr int NBARS = 4 * STAGES + 2;
+  static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
+  static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
+  static constexpr int SF_BASE = ACC_COLS;
+  static constexpr int SFBC = BN / 64;                     // B-scale columns per 64-element K block
+  static constexpr int SF_STAGE_COLS = 16 + 4 * SFBC * (DUAL ? 2 : 1);
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int THREADS = 320;
+  static constexpr bool PAIR = true;
+  static constexpr int TILE_M = 2 * BM;
+  static constexpr int B_BOX = HB;
+  static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(256, BN);
+  static constexpr uint32_t TX_AB = 2u * (A_BYTES + B_BYTES * (DUAL ? 2 : 1));   // both CTAs' operand bytes
+  static_assert(BN % 64 == 0 && BN <= 256, "pair tile N");
+  static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <class C, int MAXG>
+__global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_constant__ GemmParams<MAXG> P) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t sbase = smem_u32(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cta = cluster_ctarank();
+  const uint32_t pair = cluster_id_x(), npairs = nclusters_x();
+  if (sbase & 1023u) {  // a uniform condition: both CTAs of a pair leave together
+    if (threadIdx.x == 0) atomicOr(P.err, kDevErrTimeoutMma);
+    return;
+  }
+  const uint32_t bar_full = sbase + C::OFF_BAR;            // leader: both CTAs' operand bytes
+  const uint32_t bar_sff = bar_full + 8 * C::STAGES;       // local: this CTA's scale bytes
+  const uint32_t bar_empty = bar_sff + 8 * C::STAGES;      // local: stage consumed by the pair MMAs
+  const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;      // leader: scales of both CTAs in tensor memory
+  const uint32_t bar_accf = bar_sfr + 8 * C::STAGES;       // local: accumulator ready
+  const uint32_t bar_acce = bar_accf + 8;                  // leader: both epilogues drained
+  const uint32_t tmem_slot = bar_acce + 8;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_sff + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+      mbar_init(bar_sfr + 8 * s, 8);
+    }
+    mbar_init(bar_accf, 1);
+    mbar_init(bar_acce, 8);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish_pair();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync();   // barriers of both CTAs initialised before any cross-CTA arrival
+  tc::fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - sbase));
+
+  if (warp == 0) {
+    // --------------------------- producer (both CTAs) ---------------------------
+    if (lane == 0) {
+      for (int i = 0; i < P.ngroups; ++i) {
+        prefetch_tmap(&P.g[i].ta);
+        prefetch_tmap(&P.g[i].tb);
+        if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
+      }
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_first();
+      uint32_t it = 0;
+      for (int t = pair; t < P.total_tiles; t += npairs) {
+        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+        const int local = t - G.tile_begin;
+        const int mt = local % G.tiles_m, nt = local / G.tiles_m;
+        const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+        const int rt_a = mt * 2 + (int)cta, nrt_a = (G.M + 127) / 128, nrt_b = (G.N + 127) / 128;
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
+          const uint32_t st = sbase + s * C::STAGE_BYTES;
+          const uint32_t fb_leader = mapa(bar_full + 8 * s, 0);
+          const int nch = min(4, nk64 - 4 * ks);
+          if (cta == 0) mbar_arrive_expect_tx(bar_full + 8 * s, C::TX_AB);
+          tma_load_2d_pair(st, &G.ta, fb_leader, ks * KSTEP_BYTES, rt_a * BM, pol_a);
+          tma_load_2d_pair(st + C::OFF_B, &G.tb, fb_leader, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB, pol_b);
+          if (C::DUAL)
+            tma_load_2d_pair(st + C::OFF_B2, &G.tb2, fb_leader, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB,
+                             pol_b);
+          // scales: this CTA's A rows, all B rows of the tile
+          uint32_t sfbytes = (rt_a < nrt_a ? nch * 512 : 0);
+          for (int nb = 0; nb < C::NB; ++nb)
+            if ((nt * C::BN) / 128 + nb < nrt_b) sfbytes += nch * 512 * (C::DUAL ? 2 : 1);
+          const uint32_t sb = bar_sff + 8 * s;
+          mbar_arrive_expect_tx(sb, sfbytes);
+          if (rt_a < nrt_a) bulk_g2s(st + C::OFF_SFA, G.sfa + ((size_t)rt_a * nk64 + 4 * ks) * 512, nch * 512, sb);
+          for (int nb = 0; nb < C::NB; ++nb) {
+            const int rt = (nt * C::BN) / 128 + nb;
+            if (rt >= nrt_b) continue;
+            bulk_g2s(st + C::OFF_SFB + nb * 2048, G.sfb + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, sb);
+            if (C::DUAL)
+              bulk_g2s(st + C::OFF_SFB2 + nb * 2048, G.sfb2 + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, sb);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------ MMA (leader) ------------------------------
+    if (lane == 0 && cta == 0) {
+      const uint32_t empty0 = mapa(bar_empty, 0), empty1 = mapa(bar_empty, 1);
+      const uint32_t accf0 = mapa(bar_accf, 0), accf1 = mapa(bar_accf, 1);
+      uint32_t it = 0, tile_it = 0;
+      for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
+        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+        const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+        if (!mbar_wait_cluster(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
+        tc::fence_after_sync();
+        for (int ks = 0; ks < nks; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(bar_full + 8 * s, ph, P.err, kDevErrTimeoutFull)) goto done;
+          if (!mbar_wait_cluster(bar_sfr + 8 * s, ph, P.err, kDevErrTimeoutFull)) goto done;
+          tc::fence_after_sync();
+          const uint32_t st = sbase + s * C::STAGE_BYTES;
+          const int nch = min(4, nk64 - 4 * ks);
+          const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
+          const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFBC;
+          const uint64_t da = tc::desc_sw128(st), db = tc::desc_sw128(st + C::OFF_B);
+          const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
+          for (int kk = 0; kk < nch; ++kk) {
+            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+            tc::mma_mxf4nvf4_pair(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFBC,
+                                  accum);
+            if (C::DUAL)
+              tc::mma_mxf4nvf4_pair(tmem + C::BN, da + 2 * kk, db2 + 2 * kk, C::IDESC, sfa_t + 4 * kk,
+                                    sfb2_t + kk * C::SFBC, accum);
+          }
+          tc::commit_pair(empty0 + 8 * s);
+          tc::commit_pair(empty1 + 8 * s);
+        }
+        tc::commit_pair(accf0);
+        tc::commit_pair(accf1);
+      }
+    }
+  } else if (warp >= 6) {
+    // --------------------------- scale warps (both CTAs) ---------------------------
+    const int q = warp & 3;
+    const int half = q >> 1;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t sfr_leader = mapa(bar_sfr, 0);
+    uint32_t it = 0;
+    for (int t = pair; t < P.total_tiles; t += npairs) {
+      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+      const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+      for (int ks = 0; ks < nks; ++ks, ++it) {
+        const int s = it % C::STAGES;
+        if (!mbar_wait(bar_sff + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
+        const uint8_t* st = smem_raw + s * C::STAGE_BYTES;
+        const int nch = min(4, nk64 - 4 * ks);
+        const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
+        const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFBC;
+        for (int kk = 0; kk < nch; ++kk) {
+          const uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
+          tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
+          // B scales, pair layout: this quarter holds tile rows half*BN/2 + 32j + lane
+#pragma unroll
+          for (int op = 0; op < (C::DUAL ? 2 : 1); ++op) {
+            const uint8_t* base = st + (op ? C::OFF_SFB2 : C::OFF_SFB) + kk * 512 + lane * 16;
+            uint32_t w[4];
+#pragma unroll
+            for (int j = 0; j < C::SFBC; ++j) {
+              const int r = half * (C::BN / 2) + 32 * j;
+              w[j] = *reinterpret_cast<const uint32_t*>(base + (r / 128) * 2048 + ((r % 128) / 32) * 4);
+            }
+            const uint32_t col = (op ? sfb2_t : sfb_t) + kk * C::SFBC;
+            if constexpr (C::SFBC == 4) tc::st_32x32b_x4(col, w[0], w[1], w[2], w[3]);
+            else if constexpr (C::SFBC == 2) tc::st_32x32b_x2(col, w[0], w[1]);
+          }
+        }
+        tc::wait_st();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(sfr_leader + 8 * s);
+      }
+    }
+  } else {
+    // ----------------------------- epilogue (both CTAs) -----------------------------
+    const int sub = warp & 3;
+    const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
+    const uint32_t acce_leader = mapa(bar_acce, 0);
+    uint32_t tile_it = 0;
+    for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
+      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
+      const int local = t - G.tile_begin;
+      const int mt = local % G.tiles_m, nt = local / G.tiles_m;
+      if (!mbar_wait_cluster(bar_accf, tile_it & 1, P.err, kDevErrTimeoutMma)) break;
+      tc::fence_after_sync();
+      const int row = mt * 256 + (int)cta * BM + sub * 32 + lane;
+      __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
+#pragma unroll 1
+      for (int cb = 0; cb < C::BN / 32; ++cb) {
+        uint32_t v[32];
+        tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
+        uint32_t h[16];
+        if constexpr (C::DUAL) {
+          uint32_t u[32];
+          tc::ld_32x32b_x32(tmem + lane_base + C::BN + cb * 32, u);
+          tc::wait_ld();
+          if (cb == C::BN / 32 - 1) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acce_leader);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            h[j] = pack_h2(silu_mul(__uint_as_float(v[2 * j]), __uint_as_float(u[2 * j])),
+                           silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
+        } else {
+          tc::wait_ld();
+          if (cb == C::BN / 32 - 1) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acce_leader);
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) h[j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+        }
+        const int col0 = nt * C::BN + cb * 32;
+        if (row < G.M) {
+          if (col0 + 32 <= G.N && G.vec_ok) {
+            uint4* dst = reinterpret_cast<uint4*>(crow + cb * 32);
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) dst[qq] = make_uint4(h[4 * qq], h[4 * qq + 1], h[4 * qq + 2], h[4 * qq + 3]);
+          } else {
+            const __half* hs = reinterpret_cast<const __half*>(h);
+            for (int j = 0; j < 32 && col0 + j < G.N; ++j) crow[cb * 32 + j] = hs[j];
+          }
+        }
+      }
+    }
+  }
+done:
+  tc::fence_before_sync();
+  __syncthreads();
+  cluster_sync();   // the leader's MMAs read this CTA's shared memory until here
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+}
+
 }  // namespace
 
 namespace {
@@ -409,6 +699,50 @@ int launch_gemm(const GemmParams<MAXG>& P, cudaStream_t stream) {
   if (grid < 1) return NVFP4_OK;
   gemm_kernel<C, MAXG><<<grid, C::THREADS, C::SMEM, stream>>>(P);
   return check_launch("gemm_kernel");
+}
+
+template <class C, int MAXG>
+int launch_gemm2(const GemmParams<MAXG>& P, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto kern = gemm2_kernel<C, MAXG>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (dev >= 64) return fail(NVFP4_ERR_UNSUPPORTED, "device index out of range");
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm2)");
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n < 1) return fail(NVFP4_ERR_UNSUPPORTED, "no CTA pairs fit on this device");
+    max_pairs[dev] = n;
+    attr_set[dev] = true;
+  }
+  int pairs = max_pairs[dev];
+  if (P.total_tiles < pairs) pairs = P.total_tiles;
+  if (pairs < 1) return NVFP4_OK;
+  cfg.gridDim = dim3(2 * pairs);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm2)");
+  return check_launch("gemm2_kernel");
+}
+
+template <class C, int MAXG>
+int launch_any(const GemmParams<MAXG>& P, cudaStream_t stream) {
+  if constexpr (C::PAIR) return launch_gemm2<C, MAXG>(P, stream);
+  else return launch_gemm<C, MAXG>(P, stream);
 }
 
 int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, int box_rows) {
@@ -463,8 +797,8 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   GemmParams<1> P;
   std::memset(&P, 0, sizeof(P));
   GemmGroup& G = P.g[0];
-  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::BN)) ||
-      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::BN)))
+  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::B_BOX)) ||
+      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::B_BOX)))
     return rc;
   G.sfa = static_cast<const uint8_t*>(sfa);
   G.sfb = static_cast<const uint8_t*>(sfb1);
@@ -474,14 +808,14 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   G.vec_ok = vec_ok(c, ldc);
   G.tma_store = G.vec_ok && out_map(&G.tc, c, M, N, ldc) == NVFP4_OK;
   G.M = (int)M; G.N = (int)N; G.K = (int)K;
-  G.tiles_m = (int)((M + BM - 1) / BM);
+  G.tiles_m = (int)((M + C::TILE_M - 1) / C::TILE_M);
   G.tiles_n = (int)((N + C::BN - 1) / C::BN);
   G.tile_begin = 0;
   P.ngroups = 1;
   P.total_tiles = G.tiles_m * G.tiles_n;
   P.err = device_error_word();
   if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_dual_gemm: cannot resolve the device error word");
-  return launch_gemm<C, 1>(P, static_cast<cudaStream_t>(stream));
+  return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace nvfp4
@@ -515,7 +849,7 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
           (rc = check_operand("b", q.b, q.sfb, q.N, q.K, q.ldb)) || (rc = check_out(q.c, q.N, q.ldc)))
         return rc;
       GemmGroup& G = P.g[n];
-      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::BN)))
+      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::B_BOX)))
         return rc;
       G.sfa = static_cast<const uint8_t*>(q.sfa);
       G.sfb = static_cast<const uint8_t*>(q.sfb);
@@ -524,7 +858,7 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
       G.vec_ok = vec_ok(q.c, q.ldc);
       G.tma_store = G.vec_ok && out_map(&G.tc, q.c, q.M, q.N, q.ldc) == NVFP4_OK;
       G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
-      G.tiles_m = (int)((q.M + BM - 1) / BM);
+      G.tiles_m = (int)((q.M + C::TILE_M - 1) / C::TILE_M);
       G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
       G.tile_begin = tiles;
       tiles += G.tiles_m * G.tiles_n;
@@ -534,7 +868,7 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
     P.ngroups = n;
     P.total_tiles = tiles;
     P.err = err;
-    int rc = launch_gemm<C, MAXG>(P, static_cast<cudaStream_t>(stream));
+    int rc = launch_any<C, MAXG>(P, static_cast<cudaStream_t>(stream));
     if (rc) return rc;
   }
   return NVFP4_OK;

@@ -78,6 +78,69 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
+// ---- thread-block clusters ------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t nclusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive (release, cluster scope) on an mbarrier that may live in another CTA.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (arrivals from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t err_bit,
+                                                  uint64_t budget_ns = kWaitBudgetNs) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 15u) == 15u && globaltimer() - t0 > budget_ns) {
+      if (err) atomicOr(err, err_bit);
+      return false;
+    }
+  }
+}
+
+// 2-D tensor TMA load for a CTA pair: lands in this CTA's shared memory and
+// completes transaction bytes on the mbarrier at `bar_cluster` (the pair
+// leader's barrier).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster, int x, int y,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%3, %4}], [%2], %5;"
+      :: "r"(dst), "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy) : "memory");
+}
+
 // 1-D bulk copy global -> shared (the TMA unit's non-tensor form); completion
 // is reported as transaction bytes on `bar`.  Both addresses 16-byte aligned,
 // size a multiple of 16.
