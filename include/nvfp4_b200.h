@@ -156,7 +156,7 @@ typedef struct nvfp4_group {
 /*
  * Grouped GEMM over `num_groups` independent problems (host array of
  * descriptors; groups with M == 0 are skipped).  One persistent launch covers
- * up to 32 groups; its CTAs walk the tiles of all groups.
+ * up to 24 groups; its CTAs walk the tiles of all groups.
  */
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
 

@@ -43,6 +43,7 @@ constexpr int KSTEP_BYTES = 128;
 struct GemmGroup {
   CUtensorMap ta, tb, tb2;       // A [M, K/2], B [N, K/2] (B2 for the dual GEMM)
   CUtensorMap tc;                // C [M, N] fp16, 64-column boxes, 128-byte swizzle
+  CUtensorMap tsa, tsb, tsb2;    // blocked scales as [row tiles][K/64][128 x u32]
   const uint8_t* sfa;            // blocked scales of A, B, B2
   const uint8_t* sfb;
   const uint8_t* sfb2;
@@ -70,8 +71,9 @@ struct GemmParams {
 // EPI 1 stages the fp16 tile in shared memory and writes it with TMA stores
 // (needs BM*BN*2 bytes of shared memory); EPI 0 stores rows from registers.
 // POL picks the L2 policy of B loads: 0 evict-first, 1 normal.
-template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0>
+template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1>
 struct GemmCfg {
+  static constexpr int SFTMA = SFTMA_;   // scales by tensor-map TMA (1) or 1-D bulk copies (0)
   static constexpr int DBG = DBG_;
   static constexpr int EPI = EPI_;
   static constexpr int POL = POL_;
@@ -113,6 +115,31 @@ __device__ __forceinline__ int find_group(const GemmGroup* g, int ng, int t) {
   int i = 0;
   while (i + 1 < ng && g[i + 1].tile_begin <= t) ++i;
   return i;
+}
+
+// Scale blocks of one 256-element K step with 1-D bulk copies: the A row
+// tile and the B row tiles [rt_b, rt_b + NB).  The caller registered the
+// full-box byte count (as for tensor-map loads); bytes that are not copied
+// (blocks past the end of a matrix or of K) are completed here directly.
+template <class C>
+__device__ __forceinline__ void load_sf_bulk(uint32_t st, const GemmGroup& G, int rt_a, int rt_b, int nk64, int ks,
+                                             uint32_t bar) {
+  const int nch = min(4, nk64 - 4 * ks);
+  const int nrt_a = (G.M + 127) / 128, nrt_b = (G.N + 127) / 128;
+  uint32_t missing = 0;
+  if (rt_a < nrt_a) bulk_g2s(st + C::OFF_SFA, G.sfa + ((size_t)rt_a * nk64 + 4 * ks) * 512, nch * 512, bar);
+  missing += (rt_a < nrt_a) ? (4 - nch) * 512 : 2048;
+  for (int nb = 0; nb < C::NB; ++nb) {
+    const int rt = rt_b + nb;
+    const int ops = C::DUAL ? 2 : 1;
+    if (rt >= nrt_b) { missing += 2048 * ops; continue; }
+    bulk_g2s(st + C::OFF_SFB + nb * 2048, G.sfb + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, bar);
+    if (C::DUAL) bulk_g2s(st + C::OFF_SFB2 + nb * 2048, G.sfb2 + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, bar);
+    missing += (4 - nch) * 512 * ops;
+  }
+  if (missing) {   // complete the uncopied bytes ourselves
+    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(missing) : "memory");
+  }
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {
@@ -172,6 +199,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         prefetch_tmap(&P.g[i].ta);
         prefetch_tmap(&P.g[i].tb);
         if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
+        if (C::SFTMA) {
+          prefetch_tmap(&P.g[i].tsa);
+          prefetch_tmap(&P.g[i].tsb);
+          if (C::DUAL) prefetch_tmap(&P.g[i].tsb2);
+        }
       }
       const uint64_t pol_a = policy_evict_last();   // A tiles are re-read by every N tile
       const uint64_t pol_b = C::POL ? policy_evict_normal() : policy_evict_first();
@@ -182,18 +214,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int mt = local % G.tiles_m, nt = local / G.tiles_m;
         const int nk64 = G.K / 64;
         const int nks = (nk64 + 3) / 4;
-        const int nrt_b = (G.N + 127) / 128;
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const uint32_t fb = bar_full + 8 * s;
           const int nch = min(4, nk64 - 4 * ks);
-          int nbv = 0;
-          for (int nb = 0; nb < C::NB; ++nb) nbv += (nt * C::NB + nb < nrt_b) ? 1 : 0;
-          const uint32_t sfb_bytes = (uint32_t)(nbv * nch * 512);
-          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) + nch * 512 +
-                                 sfb_bytes * (C::DUAL ? 2 : 1);
+          // scale boxes always count in full (blocks past the end read as zeros)
+          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) +
+                                 ((C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1));
           if (C::DBG & 4) {
             mbar_arrive(fb);
             continue;
@@ -202,13 +231,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           tma_load_2d(st, &G.ta, fb, ks * KSTEP_BYTES, mt * BM, pol_a);
           tma_load_2d(st + C::OFF_B, &G.tb, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
           if (C::DUAL) tma_load_2d(st + C::OFF_B2, &G.tb2, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
-          bulk_g2s(st + C::OFF_SFA, G.sfa + ((size_t)mt * nk64 + 4 * ks) * 512, nch * 512, fb);
-          for (int nb = 0; nb < C::NB; ++nb) {
-            const int rt = nt * C::NB + nb;
-            if (rt >= nrt_b) continue;
-            bulk_g2s(st + C::OFF_SFB + nb * 2048, G.sfb + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, fb);
-            if (C::DUAL)
-              bulk_g2s(st + C::OFF_SFB2 + nb * 2048, G.sfb2 + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, fb);
+          if (!(C::DBG & 16)) {
+            if (C::SFTMA) {
+              tma_load_3d(st + C::OFF_SFA, &G.tsa, fb, 0, 4 * ks, mt, pol_a);
+              tma_load_3d(st + C::OFF_SFB, &G.tsb, fb, 0, 4 * ks, nt * C::NB, pol_b);
+              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, fb, 0, 4 * ks, nt * C::NB, pol_b);
+            } else {
+              load_sf_bulk<C>(st, G, mt, nt * C::NB, nk64, ks, fb);
+            }
           }
         }
       }
@@ -401,20 +431,25 @@ done:
 // Against the single-CTA kernel each CTA streams a third fewer bytes per FLOP
 // (B is split across the pair instead of loaded by both), which is what the
 // single-CTA kernel is limited by (shared-memory fill bandwidth per SM).
-//   * operand TMA loads use the .cta_group::2 form and complete on the
-//     leader's `full` barrier (no multicast anywhere);
-//   * scale blocks go to this CTA's shared memory (local `sf_full` barrier);
-//     four scale warps per CTA write them into this CTA's tensor memory: A
-//     scales as in the single-CTA kernel, B scales in the pair layout (scale
-//     rows [0, BN/2) in lane quarters 0-1, rows [BN/2, BN) in quarters 2-3,
-//     column j holding rows 32j..32j+31 of the half), then arrive on the
-//     leader's `sf_ready` barrier across the cluster;
+//   * each CTA loads its operand halves and its scale blocks with ordinary TMA
+//     into its own shared memory on one local barrier (`sf_full`); the paired
+//     .cta_group::2 load form, which completes on the leader's barrier,
+//     measured slower (loads-only pipeline 65.6 vs 49.3 us on config 4);
+//   * four scale warps per CTA wait for that barrier, write the scales into
+//     this CTA's tensor memory in the
+//     single-CTA arrangement (A: this CTA's 128 rows; B: all BN rows of the
+//     tile, 4 columns per 128-row block, replicated in every lane quarter),
+//     then arrive on the leader's `sf_ready` barrier across the cluster: that
+//     arrival tells the leader this CTA's whole stage is ready;
 //   * the leader commits each stage to both CTAs' `empty` barriers and each
-//     finished accumulator to both CTAs' `accf`; both CTAs' epilogue warps
-//     arrive on the leader's `acce`.
+//     finished accumulator to both CTAs' `accf` with one multicast commit; the
+//     scale warps and the epilogue warps of each CTA meet at a named barrier
+//     and send one arrival per CTA to the leader (`sf_ready`, `acce`).
 // ===========================================================================
-template <int BN_, bool DUAL_, int STAGES_>
+template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFTMA_ = 1>
 struct Gemm2Cfg {
+  static constexpr int SFTMA = SFTMA_;
+  static constexpr int DBG = DBG_;                         // tuning knob as in GemmCfg (0 in the product)
   static constexpr int BN = BN_;                           // N per pair MMA (per B operand)
   static constexpr bool DUAL = DUAL_;
   static constexpr int STAGES = STAGES_;
@@ -434,7 +469,7 @@ struct Gemm2Cfg {
   static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
   static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
   static constexpr int SF_BASE = ACC_COLS;
-  static constexpr int SFBC = BN / 64;                     // B-scale columns per 64-element K block
+  static constexpr int SFBC = NB * 4;                      // B-scale columns per 64-element K block
   static constexpr int SF_STAGE_COLS = 16 + 4 * SFBC * (DUAL ? 2 : 1);
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 320;
@@ -473,10 +508,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_sff + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
-      mbar_init(bar_sfr + 8 * s, 8);
+      mbar_init(bar_sfr + 8 * s, 2);
     }
     mbar_init(bar_accf, 1);
-    mbar_init(bar_acce, 8);
+    mbar_init(bar_acce, 2);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -496,6 +531,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
         prefetch_tmap(&P.g[i].ta);
         prefetch_tmap(&P.g[i].tb);
         if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
+        if (C::SFTMA) {
+          prefetch_tmap(&P.g[i].tsa);
+          prefetch_tmap(&P.g[i].tsb);
+          if (C::DUAL) prefetch_tmap(&P.g[i].tsb2);
+        }
       }
       const uint64_t pol_a = policy_evict_last();
       const uint64_t pol_b = policy_evict_first();
@@ -505,32 +545,31 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
         const int local = t - G.tile_begin;
         const int mt = local % G.tiles_m, nt = local / G.tiles_m;
         const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
-        const int rt_a = mt * 2 + (int)cta, nrt_a = (G.M + 127) / 128, nrt_b = (G.N + 127) / 128;
+        const int rt_a = mt * 2 + (int)cta;
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const uint32_t fb_leader = mapa(bar_full + 8 * s, 0);
           const int nch = min(4, nk64 - 4 * ks);
-          if (cta == 0) mbar_arrive_expect_tx(bar_full + 8 * s, C::TX_AB);
-          tma_load_2d_pair(st, &G.ta, fb_leader, ks * KSTEP_BYTES, rt_a * BM, pol_a);
-          tma_load_2d_pair(st + C::OFF_B, &G.tb, fb_leader, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB, pol_b);
-          if (C::DUAL)
-            tma_load_2d_pair(st + C::OFF_B2, &G.tb2, fb_leader, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB,
-                             pol_b);
-          // scales: this CTA's A rows, all B rows of the tile
-          uint32_t sfbytes = (rt_a < nrt_a ? nch * 512 : 0);
-          for (int nb = 0; nb < C::NB; ++nb)
-            if ((nt * C::BN) / 128 + nb < nrt_b) sfbytes += nch * 512 * (C::DUAL ? 2 : 1);
-          const uint32_t sb = bar_sff + 8 * s;
-          mbar_arrive_expect_tx(sb, sfbytes);
-          if (rt_a < nrt_a) bulk_g2s(st + C::OFF_SFA, G.sfa + ((size_t)rt_a * nk64 + 4 * ks) * 512, nch * 512, sb);
-          for (int nb = 0; nb < C::NB; ++nb) {
-            const int rt = (nt * C::BN) / 128 + nb;
-            if (rt >= nrt_b) continue;
-            bulk_g2s(st + C::OFF_SFB + nb * 2048, G.sfb + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, sb);
-            if (C::DUAL)
-              bulk_g2s(st + C::OFF_SFB2 + nb * 2048, G.sfb2 + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, sb);
+          if (C::DBG & 4) {
+            mbar_arrive(bar_sff + 8 * s);
+            continue;
+          }
+          // operands and scales of this CTA, all on its local barrier
+          const uint32_t lb = bar_sff + 8 * s;
+          mbar_arrive_expect_tx(lb, C::TX_AB / 2 + ((C::DBG & 16) ? 0 : 2048 + C::SFB_BYTES * (C::DUAL ? 2 : 1)));
+          tma_load_2d(st, &G.ta, lb, ks * KSTEP_BYTES, rt_a * BM, pol_a);
+          tma_load_2d(st + C::OFF_B, &G.tb, lb, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB, pol_b);
+          if (C::DUAL) tma_load_2d(st + C::OFF_B2, &G.tb2, lb, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB, pol_b);
+          if (!(C::DBG & 16)) {
+            if (C::SFTMA) {
+              tma_load_3d(st + C::OFF_SFA, &G.tsa, lb, 0, 4 * ks, rt_a, pol_a);
+              tma_load_3d(st + C::OFF_SFB, &G.tsb, lb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
+              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, lb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
+            } else {
+              load_sf_bulk<C>(st, G, rt_a, (nt * C::BN) / 128, nk64, ks, lb);
+            }
           }
         }
       }
@@ -538,8 +577,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
   } else if (warp == 1) {
     // ------------------------------ MMA (leader) ------------------------------
     if (lane == 0 && cta == 0) {
-      const uint32_t empty0 = mapa(bar_empty, 0), empty1 = mapa(bar_empty, 1);
-      const uint32_t accf0 = mapa(bar_accf, 0), accf1 = mapa(bar_accf, 1);
       uint32_t it = 0, tile_it = 0;
       for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
@@ -549,7 +586,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(bar_full + 8 * s, ph, P.err, kDevErrTimeoutFull)) goto done;
+          // both CTAs' operands landed and their scales are in tensor memory
           if (!mbar_wait_cluster(bar_sfr + 8 * s, ph, P.err, kDevErrTimeoutFull)) goto done;
           tc::fence_after_sync();
           const uint32_t st = sbase + s * C::STAGE_BYTES;
@@ -558,7 +595,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFBC;
           const uint64_t da = tc::desc_sw128(st), db = tc::desc_sw128(st + C::OFF_B);
           const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
-          for (int kk = 0; kk < nch; ++kk) {
+          for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
             tc::mma_mxf4nvf4_pair(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFBC,
                                   accum);
@@ -566,17 +603,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
               tc::mma_mxf4nvf4_pair(tmem + C::BN, da + 2 * kk, db2 + 2 * kk, C::IDESC, sfa_t + 4 * kk,
                                     sfb2_t + kk * C::SFBC, accum);
           }
-          tc::commit_pair(empty0 + 8 * s);
-          tc::commit_pair(empty1 + 8 * s);
+          tc::commit_pair_both(bar_empty + 8 * s, 3);
         }
-        tc::commit_pair(accf0);
-        tc::commit_pair(accf1);
+        tc::commit_pair_both(bar_accf, 3);
       }
     }
   } else if (warp >= 6) {
     // --------------------------- scale warps (both CTAs) ---------------------------
     const int q = warp & 3;
-    const int half = q >> 1;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     const uint32_t sfr_leader = mapa(bar_sfr, 0);
     uint32_t it = 0;
@@ -590,28 +624,25 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
         const int nch = min(4, nk64 - 4 * ks);
         const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
         const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFBC;
-        for (int kk = 0; kk < nch; ++kk) {
+        for (int kk = 0; kk < nch && !(C::DBG & 1); ++kk) {
           const uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
           tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
-          // B scales, pair layout: this quarter holds tile rows half*BN/2 + 32j + lane
+          // B scales: every 128-row block of the tile into 4 columns, in every
+          // lane quarter (the same image as for a single-CTA MMA of N = BN)
 #pragma unroll
           for (int op = 0; op < (C::DUAL ? 2 : 1); ++op) {
-            const uint8_t* base = st + (op ? C::OFF_SFB2 : C::OFF_SFB) + kk * 512 + lane * 16;
-            uint32_t w[4];
 #pragma unroll
-            for (int j = 0; j < C::SFBC; ++j) {
-              const int r = half * (C::BN / 2) + 32 * j;
-              w[j] = *reinterpret_cast<const uint32_t*>(base + (r / 128) * 2048 + ((r % 128) / 32) * 4);
+            for (int nb = 0; nb < C::NB; ++nb) {
+              const uint4 w = *reinterpret_cast<const uint4*>(st + (op ? C::OFF_SFB2 : C::OFF_SFB) + nb * 2048 +
+                                                              kk * 512 + lane * 16);
+              tc::st_32x32b_x4((op ? sfb2_t : sfb_t) + kk * C::SFBC + 4 * nb, w.x, w.y, w.z, w.w);
             }
-            const uint32_t col = (op ? sfb2_t : sfb_t) + kk * C::SFBC;
-            if constexpr (C::SFBC == 4) tc::st_32x32b_x4(col, w[0], w[1], w[2], w[3]);
-            else if constexpr (C::SFBC == 2) tc::st_32x32b_x2(col, w[0], w[1]);
           }
         }
         tc::wait_st();
         tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(sfr_leader + 8 * s);
+        asm volatile("bar.sync 3, 128;" ::: "memory");     // the 4 scale warps of this CTA
+        if (threadIdx.x == 192) mbar_arrive_cluster(sfr_leader + 8 * s);
       }
     }
   } else {
@@ -639,8 +670,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           tc::wait_ld();
           if (cb == C::BN / 32 - 1) {
             tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acce_leader);
+            asm volatile("bar.sync 4, 128;" ::: "memory");   // the 4 epilogue warps of this CTA
+            if (threadIdx.x == 64) mbar_arrive_cluster(acce_leader);
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -650,8 +681,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           tc::wait_ld();
           if (cb == C::BN / 32 - 1) {
             tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acce_leader);
+            asm volatile("bar.sync 4, 128;" ::: "memory");   // the 4 epilogue warps of this CTA
+            if (threadIdx.x == 64) mbar_arrive_cluster(acce_leader);
           }
 #pragma unroll
           for (int j = 0; j < 16; ++j) h[j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
@@ -752,6 +783,16 @@ int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t 
   return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, p, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Blocked scales viewed as u32 [row tiles][K/64 blocks][128]: a box of
+// {128, 4, n} is n row tiles x one 256-element K step (2 KB per row tile).
+int sf_map(CUtensorMap* m, const void* sf, int64_t rows, int64_t K, int box_tiles) {
+  const uint64_t nk64 = (uint64_t)(K / 64);
+  const uint64_t dims[3] = {128, nk64, (uint64_t)((rows + 127) / 128)};
+  const uint64_t str[2] = {512, nk64 * 512};
+  const uint32_t box[3] = {128, 4, (uint32_t)box_tiles};
+  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, sf, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 int check_operand(const char* name, const void* p, const void* sf, int64_t rows, int64_t K, int64_t ld) {
   if (!p || !sf) return fail(NVFP4_ERR_INVALID, "%s: null pointer", name);
   if (rows < 1) return fail(NVFP4_ERR_INVALID, "%s: need at least one row", name);
@@ -800,6 +841,9 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::B_BOX)) ||
       (rc = operand_map(&G.tb2, b2, N, K, ldb, C::B_BOX)))
     return rc;
+  if ((rc = sf_map(&G.tsa, sfa, M, K, 1)) || (rc = sf_map(&G.tsb, sfb1, N, K, C::NB)) ||
+      (rc = sf_map(&G.tsb2, sfb2, N, K, C::NB)))
+    return rc;
   G.sfa = static_cast<const uint8_t*>(sfa);
   G.sfb = static_cast<const uint8_t*>(sfb1);
   G.sfb2 = static_cast<const uint8_t*>(sfb2);
@@ -829,7 +873,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
 namespace nvfp4 {
 template <class C>
 int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
-  constexpr int MAXG = 32;
+  constexpr int MAXG = 24;
   if (!groups || num_groups < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_grouped_gemm: no groups");
   uint32_t* err = device_error_word();
   if (!err) return fail(NVFP4_ERR_CUDA, "nvfp4_grouped_gemm: cannot resolve the device error word");
@@ -851,6 +895,7 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
       GemmGroup& G = P.g[n];
       if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::B_BOX)))
         return rc;
+      if ((rc = sf_map(&G.tsa, q.sfa, q.M, q.K, 1)) || (rc = sf_map(&G.tsb, q.sfb, q.N, q.K, C::NB))) return rc;
       G.sfa = static_cast<const uint8_t*>(q.sfa);
       G.sfb = static_cast<const uint8_t*>(q.sfb);
       G.c = static_cast<__half*>(q.c);

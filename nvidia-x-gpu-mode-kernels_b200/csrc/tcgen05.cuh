@@ -51,6 +51,14 @@ __device__ __forceinline__ void commit_pair(uint32_t bar_cluster) {
                : "memory");
 }
 
+// Arrive once on the mbarrier at the same shared-memory offset in every CTA of
+// `cta_mask` when the pair's prior tcgen05 async ops of this thread finish.
+// (A commit, not a load: no data moves.)
+__device__ __forceinline__ void commit_pair_both(uint32_t bar, uint16_t cta_mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               :: "r"(bar), "h"(cta_mask) : "memory");
+}
+
 __device__ __forceinline__ void fence_before_sync() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }

@@ -81,7 +81,7 @@ def dual_gemm(a, b1, b2, scale_a, scale_b1, scale_b2, c):
 
 
 def grouped_gemm(a_list, b_list, scale_a_list, scale_b_list, c_list):
-    """c_g = a_g . b_g^T for every group g (one persistent launch for up to 32 groups)."""
+    """c_g = a_g . b_g^T for every group g (one persistent launch for up to 24 groups)."""
     G = len(a_list)
     if not (len(b_list) == len(scale_a_list) == len(scale_b_list) == len(c_list) == G) or G == 0:
         raise ValueError("grouped_gemm: all lists must have the same, non-zero length")

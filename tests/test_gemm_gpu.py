@@ -73,7 +73,7 @@ def test_grouped_gemm_empty_group_and_unaligned_ldc(pkg, oracle, cuda):
 
 
 def test_grouped_gemm_many_groups(pkg, oracle, cuda):
-    """More than one launch's worth of groups (32 per launch)."""
+    """More than one launch's worth of groups (24 per launch)."""
     _grouped(pkg, oracle, cuda, [64] * 40, 128, 128, seed=40)
 
 
