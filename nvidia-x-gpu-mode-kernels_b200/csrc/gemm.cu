@@ -81,7 +81,8 @@ struct GemmCfg {
   static constexpr int BN = BN_;
   static constexpr bool DUAL = DUAL_;
   static constexpr int STAGES = STAGES_;
-  static constexpr int NB = BN / 128;                      // 128-row scale blocks per B tile
+  static constexpr int NB = (BN + 127) / 128;              // 128-row scale blocks per B tile
+  static_assert(BN % 128 == 0 || (BN < 128 && 128 % BN == 0 && BN % 32 == 0), "B tiles must not straddle scale blocks");
   static constexpr int A_BYTES = BM * KSTEP_BYTES;         // 16 KB
   static constexpr int B_BYTES = BN * KSTEP_BYTES;
   static constexpr int SFA_BYTES = 4 * 512;                // 4 K-blocks of 64
@@ -234,10 +235,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           if (!(C::DBG & 16)) {
             if (C::SFTMA) {
               tma_load_3d(st + C::OFF_SFA, &G.tsa, fb, 0, 4 * ks, mt, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, fb, 0, 4 * ks, nt * C::NB, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, fb, 0, 4 * ks, nt * C::NB, pol_b);
+              tma_load_3d(st + C::OFF_SFB, &G.tsb, fb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
+              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, fb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
             } else {
-              load_sf_bulk<C>(st, G, mt, nt * C::NB, nk64, ks, fb);
+              load_sf_bulk<C>(st, G, mt, (nt * C::BN) / 128, nk64, ks, fb);
             }
           }
         }
@@ -251,6 +252,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
         const int nk64 = G.K / 64;
         const int nks = (nk64 + 3) / 4;
+        // a B tile narrower than 128 rows starts inside its scale block: its
+        // scales begin (tile row offset / 32) columns into the block's 4
+        const uint32_t sfb_off = (uint32_t)((((t - G.tile_begin) / G.tiles_m) * C::BN) % 128) / 32;
         if (!mbar_wait(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
         tc::fence_after_sync();
         for (int ks = 0; ks < nks; ++ks, ++it) {
@@ -278,10 +282,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
             // the k-th 64-element slice starts 32 bytes further (encoded >> 4)
             tc::mma_mxf4nvf4(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk,
-                             sfb_t + kk * C::SFB_COLS_PER_KB, accum);
+                             sfb_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
             if (C::DUAL)
               tc::mma_mxf4nvf4(tmem + C::BN, da + 2 * kk, db2 + 2 * kk, C::IDESC, sfa_t + 4 * kk,
-                               sfb2_t + kk * C::SFB_COLS_PER_KB, accum);
+                               sfb2_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
           }
           tc::commit(bar_empty + 8 * s);
         }
@@ -478,7 +482,7 @@ struct Gemm2Cfg {
   static constexpr int B_BOX = HB;
   static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(256, BN);
   static constexpr uint32_t TX_AB = 2u * (A_BYTES + B_BYTES * (DUAL ? 2 : 1));   // both CTAs' operand bytes
-  static_assert(BN % 64 == 0 && BN <= 256, "pair tile N");
+  static_assert(BN % 64 == 0 && BN <= 256 && (BN % 128 == 0 || BN == 64), "pair tile N");
   static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -581,6 +585,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
       for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
         const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+        const uint32_t sfb_off = (uint32_t)((((t - G.tile_begin) / G.tiles_m) * C::BN) % 128) / 32;
         if (!mbar_wait_cluster(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
         tc::fence_after_sync();
         for (int ks = 0; ks < nks; ++ks, ++it) {
@@ -597,11 +602,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
           for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-            tc::mma_mxf4nvf4_pair(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFBC,
-                                  accum);
+            tc::mma_mxf4nvf4_pair(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk,
+                                  sfb_t + kk * C::SFBC + sfb_off, accum);
             if (C::DUAL)
               tc::mma_mxf4nvf4_pair(tmem + C::BN, da + 2 * kk, db2 + 2 * kk, C::IDESC, sfa_t + 4 * kk,
-                                    sfb2_t + kk * C::SFBC, accum);
+                                    sfb2_t + kk * C::SFBC + sfb_off, accum);
           }
           tc::commit_pair_both(bar_empty + 8 * s, 3);
         }
