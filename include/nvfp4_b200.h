@@ -119,6 +119,22 @@ NVFP4_API int nvfp4_device_errors(uint32_t* out_bits, int clear);
  */
 NVFP4_API int nvfp4_selftest_wait_timeout(uint64_t budget_ns, void* stream);
 
+/*
+ * The same self-test without any device allocation, for callers that cannot
+ * allocate device memory (a serving process whose allocator already owns all
+ * of the GPU's memory, or a host runtime with no device-allocation hook).
+ * Launches `waiters` blocks (1..64), each waiting with budget `budget_ns` on a
+ * barrier nothing completes, and stores in *expired how many waits gave up;
+ * returns NVFP4_ERR_TIMEOUT when any did (the expected outcome), and
+ * NVFP4_ERR_INVALID for more than 64 waiters.  The outcome words live in a
+ * fixed 256-byte array inside the library that every GPU loading the library
+ * keeps until exit; the first call on a device resolves its address (make that
+ * call before any stream capture).  Calls share the array and clear the words
+ * they use, so calls that overlap on the GPU race.  Synchronises `stream`.
+ * No counterpart in the reference.
+ */
+NVFP4_API int nvfp4_selftest_wait_timeout_noalloc(uint64_t budget_ns, int waiters, int* expired, void* stream);
+
 
 /*
  * NVFP4 GEMM operands (dual and grouped GEMM): an operand with `rows` rows is

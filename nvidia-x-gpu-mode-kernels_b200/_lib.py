@@ -31,6 +31,7 @@ SIGNATURES: dict[str, list] = {
     "nvfp4_gemv": [VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_device_errors": [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int],
     "nvfp4_selftest_wait_timeout": [ctypes.c_uint64, VP],
+    "nvfp4_selftest_wait_timeout_noalloc": [ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(ctypes.c_int), VP],
     "nvfp4_version": [],
     "nvfp4_dual_gemm": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_grouped_gemm": [ctypes.POINTER(Group), ctypes.c_int, VP],

@@ -153,3 +153,94 @@ extern "C" int nvfp4_selftest_wait_timeout(uint64_t budget_ns, void* stream) {
                            (unsigned long long)budget_ns);
   return NVFP4_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free form of the bounded-wait self-test.
+//
+// nvfp4_selftest_wait_timeout allocates a 4-byte device word for each run.
+// Some callers cannot allocate device memory at all: a serving process whose
+// allocator has reserved every byte of the GPU up front, or a host runtime
+// that has no hook for device allocations, still wants to check that the
+// library's waits give up instead of hanging.  This entry point keeps the
+// words it needs in a fixed array inside the library: 64 32-bit words
+// (256 bytes), one per waiting block, resident on every GPU that loads the
+// library until the process exits.  The caller passes the budget and the
+// number of waiting blocks, and gets back how many waits expired.
+// ---------------------------------------------------------------------------
+namespace nvfp4 {
+namespace {
+
+constexpr int kSelftestMaxWaiters = 64;
+static __device__ __align__(256) uint32_t g_selftest_scratch[kSelftestMaxWaiters];
+
+uint32_t* g_selftest_ptr[kMaxDevices] = {};
+
+// Each block waits on its own mbarrier that nothing completes; thread 0
+// records 1 (completed) or 2 (expired) in word blockIdx.x of `outcome`.
+__global__ void selftest_wait_noalloc_kernel(uint32_t* err, uint64_t budget_ns, uint32_t* outcome) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(b, 0, err, kDevErrTimeoutTest, budget_ns);
+  if (threadIdx.x == 0) outcome[blockIdx.x] = ok ? 1u : 2u;
+}
+
+// Device address of this device's array, resolved once with the device
+// current (the array's name is only a host-side stand-in).
+int selftest_scratch(uint32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  if (!g_selftest_ptr[dev]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_selftest_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_selftest_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(self-test scratch)");
+      g_selftest_ptr[dev] = static_cast<uint32_t*>(p);
+    }
+  }
+  *out = g_selftest_ptr[dev];
+  return NVFP4_OK;
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+extern "C" int nvfp4_selftest_wait_timeout_noalloc(uint64_t budget_ns, int waiters, int* expired, void* stream) {
+  using namespace nvfp4;
+  if (!expired) return fail(NVFP4_ERR_INVALID, "nvfp4_selftest_wait_timeout_noalloc: null output");
+  if (waiters < 1 || waiters > kSelftestMaxWaiters)
+    return fail(NVFP4_ERR_INVALID,
+                "nvfp4_selftest_wait_timeout_noalloc: waiters must be 1..%d (the built-in scratch holds %d words), "
+                "got %d", kSelftestMaxWaiters, kSelftestMaxWaiters, waiters);
+  if (budget_ns < 1000ull) budget_ns = 1000ull;
+  if (budget_ns > 1000000000ull) budget_ns = 1000000000ull;
+  uint32_t* err = device_error_word();
+  if (!err) return fail(NVFP4_ERR_CUDA, "self-test: no device error word");
+  uint32_t* words = nullptr;
+  int rc = selftest_scratch(&words);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the array keeps the previous call's outcomes: clear the words this call uses
+  cudaError_t e = cudaMemsetAsync(words, 0, sizeof(uint32_t) * waiters, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(self-test scratch)");
+  selftest_wait_noalloc_kernel<<<waiters, 32, 0, st>>>(err, budget_ns, words);
+  rc = check_launch("selftest_wait_noalloc_kernel");
+  if (rc) return rc;
+  uint32_t h[kSelftestMaxWaiters] = {};
+  e = cudaMemcpyAsync(h, words, sizeof(uint32_t) * waiters, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "self-test readback");
+  int n = 0;
+  for (int i = 0; i < waiters; ++i) n += (h[i] == 2u) ? 1 : 0;
+  *expired = n;
+  if (n > 0) return fail(NVFP4_ERR_TIMEOUT, "self-test: %d of %d waits expired after %llu ns (expected)", n, waiters,
+                         (unsigned long long)budget_ns);
+  return NVFP4_OK;
+}
