@@ -493,7 +493,11 @@ int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullpt
     if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
     return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
   }
-  if (kb >= 2048) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
+  // widest row slice whose last stage is not mostly padding: K/2 = 7168
+  // bytes is 3.5 slices of 2 KB (a half-empty last stage per tile, 52.3 us on
+  // config 2) but exactly 7 slices of 1 KB (48.6 us)
+  auto pad = [kb](int64_t w) { return ((kb + w - 1) / w) * w - kb; };
+  if (kb >= 2048 && pad(2048) <= pad(1024)) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
   if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
   return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st, grid_out);
 }
