@@ -65,7 +65,7 @@ struct GemvArgs {
   int64_t m_off;
   uint32_t epoch;    // 1-based call count of this gather (same on every rank)
   int vec_rows;      // c_sm == 1 and 16-byte aligned row runs: whole-piece peer stores
-  int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no epoch stores
+  int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no epoch stores, 8 timestamps
 };
 
 struct GemvMaps {
@@ -162,6 +162,11 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
   }
   __syncthreads();
 
+  if ((p.dbg & 8) && p.world > 0 && blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint64_t t = globaltimer();   // tuning only: flag words 32-37 hold start / signal / done times
+    p.peer_flag[p.rank][32] = (uint32_t)t;
+    p.peer_flag[p.rank][33] = (uint32_t)(t >> 32);
+  }
   const int64_t M = p.M;
   const int nk = (int)((p.K / 2 + C::KTB - 1) / C::KTB);
   const int64_t tpl = (M + C::ROWS - 1) / C::ROWS;  // tiles per batch
@@ -291,11 +296,18 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     // holds this epoch, i.e. all rows of all ranks have landed here.
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
     if (threadIdx.x == 0) {
-      __threadfence();
+      // this CTA's stores went to other GPUs too: order them at system scope
+      // before it counts itself in, so the last CTA's release covers them
+      __threadfence_system();
       uint32_t* mine = p.peer_flag[p.rank];
       const uint32_t done = atomicAdd(mine + kCtaCounter, 1u) + 1u;
       if (done == p.epoch * gridDim.x) {
         __threadfence_system();
+        if (p.dbg & 8) {
+          const uint64_t t = globaltimer();
+          mine[34] = (uint32_t)t;
+          mine[35] = (uint32_t)(t >> 32);
+        }
         if (!(p.dbg & 4))
           for (int r = 0; r < p.world; ++r)
             asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(p.epoch)
@@ -311,6 +323,11 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
               break;
             }
           }
+        }
+        if (p.dbg & 8) {
+          const uint64_t t = globaltimer();
+          mine[36] = (uint32_t)t;
+          mine[37] = (uint32_t)(t >> 32);
         }
         __threadfence_system();
       }
