@@ -310,7 +310,9 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
         }
         if (!(p.dbg & 4))
           for (int r = 0; r < p.world; ++r)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(p.epoch)
+            // relaxed: the system fence above already orders every row store
+            // before these; a release per store would fence (and wait) per peer
+            asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(p.epoch)
                          : "memory");
         const uint64_t t0 = globaltimer();
         for (int r = 0; r < p.world && !(p.dbg & 2); ++r) {
