@@ -177,6 +177,20 @@ typedef struct nvfp4_group {
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
 
 /*
+ * Fused NVFP4 quantiser for GEMM activations: x [M, K] fp16 (row stride ldx
+ * elements, K % 16 == 0) -> codes [M, K/2] (row stride ldq bytes) and e4m3
+ * scales written straight into the 128x4 blocked layout (buffer of
+ * ceil(M/128) * ceil(K/64) * 512 bytes; padding bytes are written as 0).
+ * Per 16-element block, global scale 1.0:  s = e4m3_rne_satfinite(amax / 6),
+ * q_i = e2m1_rne_satfinite(x_i / s) with IEEE f32 division; a block whose s is
+ * 0 gets all-zero codes.  Finite inputs.  No counterpart in the reference
+ * (its inputs arrive already quantised); it produces the operands of
+ * nvfp4_dual_gemm / nvfp4_grouped_gemm.
+ */
+NVFP4_API int nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, void* codes, int64_t ldq,
+                             void* sf_blocked, void* stream);
+
+/*
  * Tensor-core peak probe: one CTA per SM issues `iters` dense 128x256x64
  * kind::mxf4nvf4 MMAs (4,194,304 FLOP each) from shared memory.  Time it with
  * events on `stream` to get the device's FP4 tensor throughput, the

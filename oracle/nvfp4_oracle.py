@@ -218,3 +218,64 @@ def grouped_gemm(groups, acc=np.float32):
         r = gemm(a, b, sfa, sfb, M, N, K, acc)
         outs.append(r.astype(np.float16) if acc == np.float32 else r)
     return outs
+
+
+# ---------------------------------------------------------------------------
+# Quantiser (north-star "next" row: fp16 activations -> NVFP4).  No reference
+# code exists; these are the rounding rules the library documents.
+# ---------------------------------------------------------------------------
+
+def _round_half_even(v: np.ndarray) -> np.ndarray:
+    return np.round(v)   # numpy rounds halves to even
+
+
+def e4m3_rne_satfinite(v: np.ndarray) -> np.ndarray:
+    """Non-negative float64 -> e4m3fn byte, round-to-nearest-even, saturating
+    at 448 (the largest finite value)."""
+    v = np.asarray(v, dtype=np.float64)
+    out = np.zeros(v.shape, dtype=np.uint8)
+    pos = v > 0
+    e = np.floor(np.log2(np.where(pos, v, 1.0)))
+    e = np.clip(e, -6, 8)                                   # subnormals share the 2^-6 binade's spacing
+    spacing = 2.0 ** (e - 3)
+    q = _round_half_even(v / spacing) * spacing              # may step into the next binade: still exact
+    q = np.minimum(q, 448.0)
+    # encode q
+    qe = np.floor(np.log2(np.where(q > 0, q, 1.0)))
+    normal = q >= 2.0 ** -6
+    exp_field = np.where(normal, qe + 7, 0).astype(np.int64)
+    mant = np.where(normal, q / 2.0 ** qe - 1.0, q / 2.0 ** -6) * 8
+    code = (exp_field << 3) | np.round(mant).astype(np.int64)
+    out[pos] = code[pos].astype(np.uint8)
+    return out
+
+
+_E2M1_POS = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def e2m1_rne_satfinite(v: np.ndarray) -> np.ndarray:
+    """float -> e2m1 code (sign bit 3), round-to-nearest-even, |v| > 6 -> 6."""
+    v = np.asarray(v, dtype=np.float64)
+    a = np.minimum(np.abs(v), 6.0)
+    idx = np.searchsorted(_E2M1_POS, a)                      # first grid point >= a
+    idx = np.clip(idx, 1, 7)
+    lo, hi = _E2M1_POS[idx - 1], _E2M1_POS[idx]
+    mag = np.where(a - lo < hi - a, idx - 1, np.where(a - lo > hi - a, idx, np.where((idx - 1) % 2 == 0, idx - 1, idx)))
+    mag = np.where(a == 0, 0, mag)
+    return (mag | np.where(np.signbit(v), 8, 0)).astype(np.uint8)
+
+
+def quantize(x) -> tuple[np.ndarray, np.ndarray]:
+    """x [M, K] fp16 -> (codes [M, K/2] uint8, blocked scale bytes)."""
+    x = np.asarray(x, dtype=np.float16).astype(np.float32)
+    M, K = x.shape
+    blocks = x.reshape(M, K // 16, 16)
+    amax = np.abs(blocks).max(axis=2)
+    sbyte = e4m3_rne_satfinite((amax / np.float32(6.0)).astype(np.float32).astype(np.float64))
+    s = E4M3_LUT[sbyte].astype(np.float32)
+    safe = np.where(s > 0, s, np.float32(1.0))
+    qv = (blocks / safe[:, :, None]).astype(np.float32)     # IEEE f32 division
+    codes = e2m1_rne_satfinite(qv.astype(np.float64))
+    codes = np.where((s > 0)[:, :, None], codes, 0).astype(np.uint8).reshape(M, K)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    return packed, to_blocked_ref(sbyte)
