@@ -71,9 +71,14 @@ struct GemmParams {
 // EPI 1 stages the fp16 tile in shared memory and writes it with TMA stores
 // (needs BM*BN*2 bytes of shared memory); EPI 0 stores rows from registers.
 // POL picks the L2 policy of B loads: 0 evict-first, 1 normal.
-template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1>
+// SEPSF 1: the stage's scale boxes complete on their own barrier, issued
+// before the operand boxes, so the scale warps stage them while the operand
+// bytes are still in flight (needs SFST and SFTMA).
+template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1,
+          int SEPSF_ = 1>
 struct GemmCfg {
   static constexpr int SFTMA = SFTMA_;   // scales by tensor-map TMA (1) or 1-D bulk copies (0)
+  static constexpr int SEPSF = (SEPSF_ && SFST_ && SFTMA_) ? 1 : 0;
   static constexpr int DBG = DBG_;
   static constexpr int EPI = EPI_;
   static constexpr int POL = POL_;
@@ -96,7 +101,7 @@ struct GemmCfg {
   static constexpr int OFF_C = STAGES * STAGE_BYTES;      // fp16 output tile, BN/64 swizzled boxes
   static constexpr int C_BYTES = EPI ? BM * BN * 2 : 0;
   static constexpr int OFF_BAR = OFF_C + C_BYTES;
-  static constexpr int SMEM = OFF_BAR + (3 * STAGES + 4) * 8 + 16;   // base is 1024-aligned
+  static constexpr int SMEM = OFF_BAR + (4 * STAGES + 4) * 8 + 16;   // base is 1024-aligned
   // tensor memory columns
   static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
   static constexpr int SF_BASE = ACC_COLS;
@@ -166,7 +171,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
   const uint32_t bar_full = sbase + C::OFF_BAR;
   const uint32_t bar_empty = bar_full + 8 * C::STAGES;
   const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;      // scales in tensor memory (SFST)
-  const uint32_t bar_accf = bar_sfr + 8 * C::STAGES;
+  const uint32_t bar_sff = bar_sfr + 8 * C::STAGES;        // scale boxes landed (SEPSF)
+  const uint32_t bar_accf = bar_sff + 8 * C::STAGES;
   const uint32_t bar_acce = bar_accf + 8;
   const uint32_t bar_done = bar_acce + 8;
   const uint32_t tmem_slot = bar_done + 8;
@@ -178,6 +184,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
       mbar_init(bar_sfr + 8 * s, 4);
+      mbar_init(bar_sff + 8 * s, 1);
     }
     mbar_init(bar_accf, 1);
     mbar_init(bar_acce, 4);
@@ -222,17 +229,27 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           const uint32_t fb = bar_full + 8 * s;
           const int nch = min(4, nk64 - 4 * ks);
           // scale boxes always count in full (blocks past the end read as zeros)
-          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) +
-                                 ((C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1));
+          const uint32_t sf_bytes = (C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1);
+          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) + (C::SEPSF ? 0 : sf_bytes);
           if (C::DBG & 4) {
             mbar_arrive(fb);
+            if (C::SEPSF) mbar_arrive(bar_sff + 8 * s);
             continue;
+          }
+          if (C::SEPSF) {   // scales first, on their own barrier
+            const uint32_t sb = bar_sff + 8 * s;
+            mbar_arrive_expect_tx(sb, sf_bytes);
+            if (!(C::DBG & 16)) {
+              tma_load_3d(st + C::OFF_SFA, &G.tsa, sb, 0, 4 * ks, mt, pol_a);
+              tma_load_3d(st + C::OFF_SFB, &G.tsb, sb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
+              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, sb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
+            }
           }
           mbar_arrive_expect_tx(fb, bytes);
           tma_load_2d(st, &G.ta, fb, ks * KSTEP_BYTES, mt * BM, pol_a);
           tma_load_2d(st + C::OFF_B, &G.tb, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
           if (C::DUAL) tma_load_2d(st + C::OFF_B2, &G.tb2, fb, ks * KSTEP_BYTES, nt * C::BN, pol_b);
-          if (!(C::DBG & 16)) {
+          if (!(C::DBG & 16) && !C::SEPSF) {
             if (C::SFTMA) {
               tma_load_3d(st + C::OFF_SFA, &G.tsa, fb, 0, 4 * ks, mt, pol_a);
               tma_load_3d(st + C::OFF_SFB, &G.tsb, fb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
@@ -261,6 +278,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           const int s = it % C::STAGES;
           if (!mbar_wait((C::SFST ? bar_sfr : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull))
             goto done;
+          if (C::SEPSF && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
           tc::fence_after_sync();
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const int nch = min(4, nk64 - 4 * ks);
@@ -306,7 +324,9 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       const int nks = (nk64 + 3) / 4;
       for (int ks = 0; ks < nks; ++ks, ++it) {
         const int s = it % C::STAGES;
-        if (!dead && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) dead = true;
+        if (!dead && !mbar_wait((C::SEPSF ? bar_sff : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err,
+                                kDevErrTimeoutFull))
+          dead = true;
         if (dead) break;
         const uint8_t* st = smem_raw + (sbase - raw) + s * C::STAGE_BYTES;
         const int nch = min(4, nk64 - 4 * ks);
