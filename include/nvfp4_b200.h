@@ -88,7 +88,10 @@ NVFP4_API int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid);
  * word `rank` of every rank's buffer and waits until this rank's words 0..world-1
  * all hold `epoch`, so the launch ends with every rank's rows present locally.
  * `epoch` is the 1-based count of calls made with these flag buffers (the same
- * on every rank; the shape must stay the same between calls).  The wait is
+ * on every rank; the shape must stay the same between calls).  epoch == 0
+ * selects device-epoch mode: the kernel keeps the count in word 20 of this
+ * rank's flag buffer, so a captured CUDA graph of the call advances it on every
+ * replay (use one mode per set of flag buffers).  The wait is
  * bounded (2 s, error bit 4 in nvfp4_device_errors()).  Requires the aligned
  * (TMA) path; world <= 8.  Replaces "nvfp4_gemv_forward + an output
  * all-gather" (the reference has no distributed code; the north star asks for

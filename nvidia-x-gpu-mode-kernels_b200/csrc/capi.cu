@@ -2,6 +2,7 @@
 // that bounded waits report into, and the bounded-wait self-test kernel.
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include "ptx.cuh"
 #include "common.h"
 #include "tmap.h"
@@ -83,9 +84,53 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 }  // namespace
 
+namespace {
+// Cache of encoded tensor maps keyed by every encoding argument (a map depends
+// on nothing else), so repeated calls on the same buffers skip the driver.
+struct TmapKey {
+  const void* base;
+  uint64_t dims[5];
+  uint64_t strides[4];
+  uint32_t box[5];
+  int dtype, rank, swizzle, promo;
+  bool operator==(const TmapKey& o) const { return std::memcmp(this, &o, sizeof(TmapKey)) == 0; }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    const uint64_t* w = reinterpret_cast<const uint64_t*>(&k);
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < sizeof(TmapKey) / 8; ++i) h = (h ^ w[i]) * 1099511628211ull;
+    return (size_t)h;
+  }
+};
+std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmap_cache;
+std::mutex g_tmap_mu;
+constexpr size_t kTmapCacheMax = 4096;
+}  // namespace
+
 int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo) {
+  TmapKey key;
+  std::memset(&key, 0, sizeof(key));
+  key.base = base;
+  key.dtype = (int)dtype;
+  key.rank = rank;
+  key.swizzle = (int)swizzle;
+  key.promo = (int)promo;
+  for (int i = 0; i < rank && i < 5; ++i) {
+    key.dims[i] = dims[i];
+    key.box[i] = box[i];
+    if (i + 1 < rank) key.strides[i] = strides_bytes[i];
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_tmap_mu);
+    auto it = g_tmap_cache.find(key);
+    if (it != g_tmap_cache.end()) {
+      *map = it->second;
+      return NVFP4_OK;
+    }
+  }
   auto fn = encode_fn();
   if (!fn) return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   cuuint64_t gd[5], gs[4];
@@ -101,6 +146,9 @@ int encode_tmap(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const voi
   if (r != CUDA_SUCCESS)
     return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): rank %d dims[0]=%llu box[0]=%u", (int)r,
                 rank, (unsigned long long)dims[0], box[0]);
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  if (g_tmap_cache.size() >= kTmapCacheMax) g_tmap_cache.clear();
+  g_tmap_cache.emplace(key, *map);
   return NVFP4_OK;
 }
 

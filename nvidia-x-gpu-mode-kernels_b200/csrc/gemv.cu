@@ -44,6 +44,7 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 constexpr int kCtaCounter = 16;   // flag-buffer word counting this rank's finished CTAs
+constexpr int kEpochWord = 20;    // flag-buffer word holding the last epoch (device-epoch mode)
 
 __host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
@@ -161,6 +162,13 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     fence_mbar_init();
   }
   __syncthreads();
+  // Launched with programmatic dependent launch: everything above overlapped
+  // the previous kernel on the stream; wait for it before touching global
+  // memory (a no-op when launched without the attribute).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  uint32_t epoch_at_start = 0;
+  if (p.world > 0 && p.epoch == 0 && threadIdx.x == 0)
+    epoch_at_start = *reinterpret_cast<volatile uint32_t*>(p.peer_flag[p.rank] + kEpochWord) + 1u;
 
   if ((p.dbg & 8) && p.world > 0 && blockIdx.x == 0 && threadIdx.x == 0) {
     const uint64_t t = globaltimer();   // tuning only: flag words 32-37 hold start / signal / done times
@@ -296,12 +304,16 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     // holds this epoch, i.e. all rows of all ranks have landed here.
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
     if (threadIdx.x == 0) {
+      // epoch 0 = device-epoch mode: this launch is number (stored + 1).  Every
+      // CTA reads the word before the last CTA (which counts in after all the
+      // others have started) stores the new value.
+      const uint32_t epoch = p.epoch ? p.epoch : epoch_at_start;
       // this CTA's stores went to other GPUs too: order them at system scope
       // before it counts itself in, so the last CTA's release covers them
       __threadfence_system();
       uint32_t* mine = p.peer_flag[p.rank];
       const uint32_t done = atomicAdd(mine + kCtaCounter, 1u) + 1u;
-      if (done == p.epoch * gridDim.x) {
+      if (done == epoch * gridDim.x) {
         __threadfence_system();
         if (p.dbg & 8) {
           const uint64_t t = globaltimer();
@@ -312,14 +324,14 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
           for (int r = 0; r < p.world; ++r)
             // relaxed: the system fence above already orders every row store
             // before these; a release per store would fence (and wait) per peer
-            asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(p.epoch)
+            asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(epoch)
                          : "memory");
         const uint64_t t0 = globaltimer();
         for (int r = 0; r < p.world && !(p.dbg & 2); ++r) {
           for (uint32_t it = 0;; ++it) {
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
-            if ((int32_t)(v - p.epoch) >= 0) break;
+            if ((int32_t)(v - epoch) >= 0) break;
             if ((it & 63u) == 63u && globaltimer() - t0 > kWaitBudgetNs) {
               atomicOr(p.err, kDevErrTimeoutPeer);
               break;
@@ -331,6 +343,7 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
           mine[36] = (uint32_t)t;
           mine[37] = (uint32_t)(t >> 32);
         }
+        if (p.epoch == 0) mine[kEpochWord] = epoch;
         __threadfence_system();
       }
     }
@@ -487,7 +500,18 @@ int launch_tma(const GemvArgs& p, cudaStream_t stream, int64_t* grid_out) {
   int rc = cached_maps<C>(p, maps);
   if (rc) return rc;
   const int64_t grid = grid_of<C>(p);
-  gemv_tma_kernel<C><<<(unsigned)grid, C::THREADS, C::SMEM, stream>>>(maps, p);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_tma_kernel<C>, maps, p);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemv)");
   return check_launch("gemv_tma_kernel");
 }
 
@@ -572,7 +596,6 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
                                     uint32_t* const* peer_flags, int world, int rank, uint32_t epoch,
                                     void* stream) {
   using namespace nvfp4;
-  if (epoch == 0) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: epoch counts calls from 1");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_flags)
     return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: need 1 <= world <= %d and 0 <= rank < world", kMaxRanks);
   for (int r = 0; r < world; ++r)

@@ -145,9 +145,12 @@ class FusedShardedGemv:
     with a running epoch, so one instance serves one fixed shape.
     """
 
-    def __init__(self, M: int, K: int, L: int, group=None, device=None):
+    def __init__(self, M: int, K: int, L: int, group=None, device=None, device_epoch: bool = False):
+        """device_epoch=True keeps the call count on the GPU, so calls can be
+        captured in a CUDA graph and replayed."""
         import ctypes
         import torch.distributed._symmetric_memory as symm
+        self.device_epoch = device_epoch
         from . import _lib
         self.M, self.K, self.L = M, K, L
         self.group = group or dist.group.WORLD
@@ -175,7 +178,7 @@ class FusedShardedGemv:
 
     def __call__(self, a_rows, b, sfa_rows, sfb) -> torch.Tensor:
         from . import _lib
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        self.epoch = 0 if self.device_epoch else ((self.epoch + 1) & 0xFFFFFFFF or 1)
         sa, sb, ssa, ssb = a_rows.stride(), b.stride(), sfa_rows.stride(), sfb.stride()
         _lib.check(_lib.lib().nvfp4_gemv_allgather(
             a_rows.data_ptr(), b.data_ptr(), sfa_rows.data_ptr(), sfb.data_ptr(),

@@ -37,6 +37,25 @@ def main():
         assert pkg._lib.device_errors() == 0, "device error word set"
         assert torch.equal(got, nccl), f"fused vs NCCL mismatch at M={M} K={K} L={L}"
         assert torch.allclose(got, ref, rtol=1e-2, atol=1e-2), f"sharded vs single-GPU mismatch {M} {K} {L}"
+        # device-epoch mode, captured once in a CUDA graph and replayed
+        gfused = pkg.sharded.FusedShardedGemv(M, K, L, device_epoch=True)
+        gfused(a, full.b, sfa, full.sfb)                   # eager call (also sets up the launch)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph):
+                gfused(a, full.b, sfa, full.sfb)
+        torch.cuda.synchronize()
+        for _ in range(3):
+            gfused.out_flat.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(gfused.out().float(), nccl), f"graph replay mismatch {M} {K} {L}"
+        assert pkg._lib.device_errors() == 0, "device error word set after graph replays"
         dist.barrier()
     print(f"RANK {rank} OK", flush=True)
     dist.destroy_process_group()
