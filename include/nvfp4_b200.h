@@ -180,6 +180,18 @@ typedef struct nvfp4_group {
 NVFP4_API int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
 
 /*
+ * Skinny GEMM for decode batches: out[T, N] = x[T, K] . w[N, K]^T with
+ * 1 <= T <= 64 token rows (operand conventions as above; out row stride ldo
+ * elements).  The weights stream through the tensor cores as the MMA's
+ * 128-row operand ("swap-AB"), the tokens form one 16/32/64-wide tile, and
+ * the epilogue writes the transposed accumulator.  One CTA per 128 weight
+ * rows.  No counterpart in the reference.
+ */
+NVFP4_API int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, const void* sfw, void* out,
+                                int64_t T, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldo,
+                                void* stream);
+
+/*
  * Fused NVFP4 quantiser for GEMM activations: x [M, K] fp16 (row stride ldx
  * elements, K % 16 == 0) -> codes [M, K/2] (row stride ldq bytes) and e4m3
  * scales written straight into the 128x4 blocked layout (buffer of

@@ -7,11 +7,12 @@ directory name is not a Python identifier).
   the operator of the reference (blackwell_nvfp4_gemv.cu:500-524).
 * ``dual_gemm(a, b1, b2, scale_a, scale_b1, scale_b2, c)`` - silu(a.b1^T)*(a.b2^T).
 * ``grouped_gemm(a_list, b_list, scale_a_list, scale_b_list, c_list)``.
+* ``skinny_gemm(x, w, scale_x, scale_w, out)`` - decode-batch GEMM (1..64 rows).
 * ``quantize(x)`` - fp16 activations to e2m1 codes + blocked e4m3 scales.
 """
 from . import _lib, gemm, gemv, inputs, layout, quant, sharded  # noqa: F401
 from .quant import quantize  # noqa: F401
-from .gemm import dual_gemm, grouped_gemm  # noqa: F401
+from .gemm import dual_gemm, grouped_gemm, skinny_gemm  # noqa: F401
 from .gemv import custom_kernel  # noqa: F401
 
-__all__ = ["custom_kernel", "dual_gemm", "grouped_gemm", "quantize", "gemm", "gemv", "inputs", "layout", "quant", "sharded"]
+__all__ = ["custom_kernel", "dual_gemm", "grouped_gemm", "skinny_gemm", "quantize", "gemm", "gemv", "inputs", "layout", "quant", "sharded"]

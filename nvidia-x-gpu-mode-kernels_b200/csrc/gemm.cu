@@ -74,9 +74,12 @@ struct GemmParams {
 // SEPSF 1: the stage's scale boxes complete on their own barrier, issued
 // before the operand boxes, so the scale warps stage them while the operand
 // bytes are still in flight (needs SFST and SFTMA).
+// TRANS 1 (skinny GEMM): A holds weight rows, B the token rows, and the
+// epilogue writes C^T, i.e. out[token][weight row]; one N tile only.
 template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1,
-          int SEPSF_ = 1>
+          int SEPSF_ = 1, int TRANS_ = 0>
 struct GemmCfg {
+  static constexpr int TRANS = TRANS_;
   static constexpr int SFTMA = SFTMA_;   // scales by tensor-map TMA (1) or 1-D bulk copies (0)
   static constexpr int SEPSF = (SEPSF_ && SFST_ && SFTMA_) ? 1 : 0;
   static constexpr int DBG = DBG_;
@@ -87,7 +90,8 @@ struct GemmCfg {
   static constexpr bool DUAL = DUAL_;
   static constexpr int STAGES = STAGES_;
   static constexpr int NB = (BN + 127) / 128;              // 128-row scale blocks per B tile
-  static_assert(BN % 128 == 0 || (BN < 128 && 128 % BN == 0 && BN % 32 == 0), "B tiles must not straddle scale blocks");
+  static_assert(BN % 128 == 0 || (BN < 128 && 128 % BN == 0 && (BN % 32 == 0 || (TRANS_ && BN == 16))),
+                "B tiles must not straddle scale blocks");
   static constexpr int A_BYTES = BM * KSTEP_BYTES;         // 16 KB
   static constexpr int B_BYTES = BN * KSTEP_BYTES;
   static constexpr int SFA_BYTES = 4 * 512;                // 4 K-blocks of 64
@@ -365,6 +369,32 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       tc::fence_after_sync();
       const int rloc = sub * 32 + lane;        // row of the tile held by this thread
       const int row = mt * BM + rloc;
+      if constexpr (C::TRANS) {
+        // C^T: this thread's accumulator row is output column `row`; its BN
+        // columns are tokens.  A warp stores 32 consecutive output columns of
+        // one token per instruction.
+        constexpr int CHUNK = C::BN < 32 ? C::BN : 32;
+#pragma unroll 1
+        for (int cb = 0; cb < C::BN / CHUNK; ++cb) {
+          uint32_t v[32];
+          if constexpr (CHUNK == 32) tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
+          else tc::ld_32x32b_x16(tmem + lane_base + cb * CHUNK, v);
+          tc::wait_ld();
+          if (cb == C::BN / CHUNK - 1) {
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_acce);
+          }
+          if (row < G.M) {
+#pragma unroll
+            for (int j = 0; j < CHUNK; ++j) {
+              const int tok = nt * C::BN + cb * CHUNK + j;
+              if (tok < G.N) G.c[(int64_t)tok * G.ldc + row] = __float2half_rn(__uint_as_float(v[j]));
+            }
+          }
+        }
+        continue;
+      }
       if (C::EPI && G.tma_store) {
         // previous tile's TMA stores must have finished reading the staging tile
         if (threadIdx.x == 64) bulk_wait_read_all();
@@ -896,6 +926,38 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
 }
 
 namespace nvfp4 {
+// out[T, N] = X[T, K] . W[N, K]^T for T <= BN tokens: W streams as the MMA's A
+// operand (128 weight rows per tile), X is one BN-row B tile, C^T epilogue.
+template <class C>
+int skinny_run(const void* x, const void* w, const void* sfx, const void* sfw, void* out, int64_t T, int64_t N,
+               int64_t K, int64_t ldx, int64_t ldw, int64_t ldo, void* stream) {
+  if (K < 64 || K % 64) return fail(NVFP4_ERR_INVALID, "nvfp4_gemm_skinny: K must be a positive multiple of 64");
+  int rc;
+  if ((rc = check_operand("x", x, sfx, T, K, ldx)) || (rc = check_operand("w", w, sfw, N, K, ldw)) ||
+      (rc = check_out(out, N, ldo)))
+    return rc;
+  GemmParams<1> P;
+  std::memset(&P, 0, sizeof(P));
+  GemmGroup& G = P.g[0];
+  if ((rc = operand_map(&G.ta, w, N, K, ldw, BM)) || (rc = operand_map(&G.tb, x, T, K, ldx, C::BN)) ||
+      (rc = sf_map(&G.tsa, sfw, N, K, 1)) || (rc = sf_map(&G.tsb, sfx, T, K, 1)))
+    return rc;
+  G.sfa = static_cast<const uint8_t*>(sfw);
+  G.sfb = static_cast<const uint8_t*>(sfx);
+  G.c = static_cast<__half*>(out);
+  G.ldc = ldo;
+  G.M = (int)N;
+  G.N = (int)T;
+  G.K = (int)K;
+  G.tiles_m = (int)((N + BM - 1) / BM);
+  G.tiles_n = 1;
+  P.ngroups = 1;
+  P.total_tiles = G.tiles_m;
+  P.err = device_error_word();
+  if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_gemm_skinny: cannot resolve the device error word");
+  return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
+}
+
 template <class C>
 int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
   constexpr int MAXG = 24;
@@ -947,6 +1009,15 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
 
 extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream) {
   return grouped_run<GemmCfg<256, false, 4, 0, 1, 0, 0>>(groups, num_groups, stream);
+}
+
+extern "C" int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, const void* sfw, void* out,
+                                 int64_t T, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldo,
+                                 void* stream) {
+  if (T < 1 || T > 64) return fail(NVFP4_ERR_INVALID, "nvfp4_gemm_skinny: 1..64 token rows (got %lld)", (long long)T);
+  if (T <= 16) return skinny_run<GemmCfg<16, false, 7, 0, 1, 0, 0, 1, 1, 1>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+  if (T <= 32) return skinny_run<GemmCfg<32, false, 7, 0, 1, 0, 0, 1, 1, 1>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+  return skinny_run<GemmCfg<64, false, 7, 0, 1, 0, 0, 1, 1, 1>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -105,3 +105,25 @@ def grouped_gemm(a_list, b_list, scale_a_list, scale_b_list, c_list):
     with torch.cuda.device(dev):
         _lib.check(_lib.lib().nvfp4_grouped_gemm(arr, G, _stream(dev)))
     return c_list
+
+
+def skinny_gemm(x, w, scale_x, scale_w, out):
+    """out[T, N] = x[T, K] . w[N, K]^T for a decode batch of 1 <= T <= 64 token
+    rows; the weights stream through the tensor cores as the 128-row MMA
+    operand."""
+    _codes("x", x)
+    T, K = x.shape[0], x.shape[1] * 2
+    _codes("w", w)
+    N = w.shape[0]
+    if w.shape[1] * 2 != K:
+        raise ValueError("x and w disagree on K")
+    if not 1 <= T <= 64:
+        raise ValueError("skinny_gemm takes 1..64 token rows; use grouped_gemm for more")
+    sx = _scales("scale_x", scale_x, T, K)
+    sw = _scales("scale_w", scale_w, N, K)
+    _out(out, T, N)
+    with torch.cuda.device(out.device):
+        _lib.check(_lib.lib().nvfp4_gemm_skinny(x.data_ptr(), w.data_ptr(), sx.data_ptr(), sw.data_ptr(),
+                                                out.data_ptr(), T, N, K, x.stride(0), w.stride(0), out.stride(0),
+                                                _stream(out.device)))
+    return out

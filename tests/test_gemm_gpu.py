@@ -106,3 +106,22 @@ def test_mma_peak_probe_runs(pkg, cuda):
     pkg._lib.check(pkg._lib.lib().nvfp4_mma_peak(64, s))
     torch.cuda.synchronize()
     assert pkg._lib.device_errors() == 0
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (8, 14336, 4096), (16, 1000, 512), (17, 640, 256), (64, 256, 1024),
+                                   (3, 130, 64)])
+def test_skinny_gemm(pkg, oracle, cuda, T, N, K):
+    x, w = _ops(pkg, [T, N], K, seed=T * 31 + N)
+    out = torch.full((T, N), float("nan"), dtype=torch.float16, device=cuda)
+    pkg.skinny_gemm(x.codes.to(cuda), w.codes.to(cuda), x.sf_blocked.to(cuda), w.sf_blocked.to(cuda), out)
+    torch.cuda.synchronize()
+    assert pkg._lib.device_errors() == 0
+    ref = oracle.gemm(x.codes, w.codes, x.sf_blocked, w.sf_blocked, T, N, K).astype(np.float16)
+    _close(out.cpu().numpy(), ref)
+
+
+def test_skinny_gemm_rejects_too_many_rows(pkg, cuda):
+    x, w = _ops(pkg, [65, 128], 64, seed=3)
+    out = torch.empty((65, 128), dtype=torch.float16, device=cuda)
+    with pytest.raises(ValueError):
+        pkg.skinny_gemm(x.codes.to(cuda), w.codes.to(cuda), x.sf_blocked.to(cuda), w.sf_blocked.to(cuda), out)
