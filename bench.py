@@ -309,6 +309,37 @@ def run_grouped_extra(pkg, flush, steps, warmup, peak_tf, hbm):
             "gbs": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4)}
 
 
+def run_skinny_extra(pkg, flush, steps, warmup, hbm, T=16, N=14336, K=4096):
+    g = torch.Generator().manual_seed(0)
+    x, w = pkg.inputs.operand(T, K, g, device="cuda"), pkg.inputs.operand(N, K, g, device="cuda")
+    out = torch.empty((T, N), dtype=torch.float16, device="cuda")
+
+    def step(ev):
+        ev_mark(ev)
+        pkg.skinny_gemm(x.codes, w.codes, x.sf_blocked, w.sf_blocked, out)
+        ev_mark(ev)
+
+    t = statistics.mean(s[0] for s in time_steps(step, steps, warmup, flush)) * 1e-3
+    nbytes = (T + N) * K // 2 + (T + N) * K // 16 + 2 * T * N
+    return {"workload": f"skinny gemm T={T} N={N} K={K} (decode batch, weights streamed)", "us": round(t * 1e6, 3),
+            "gbs": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4)}
+
+
+def run_quant_extra(pkg, flush, steps, warmup, hbm, M=8192, K=7168):
+    x = torch.randn((M, K), device="cuda").to(torch.float16)
+    codes, sf = pkg.quantize(x)
+
+    def step(ev):
+        ev_mark(ev)
+        pkg.quantize(x, codes, sf)
+        ev_mark(ev)
+
+    t = statistics.mean(s[0] for s in time_steps(step, steps, warmup, flush)) * 1e-3
+    nbytes = M * K * 2 + M * K // 2 + M * K // 16
+    return {"workload": f"quantize fp16 -> nvfp4 M={M} K={K}", "us": round(t * 1e6, 3),
+            "gbs": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4)}
+
+
 def our_arm(args, world, rank, local):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
@@ -438,7 +469,9 @@ def our_arm(args, world, rank, local):
             peak_tf = fp4_peak_tflops(pkg)
             line["fp4_peak_tflops_measured"] = round(peak_tf, 1)
             line["extras"] += [run_dual_extra(pkg, flush, 30, 3, peak_tf, pk["hbm_gbs"]),
-                               run_grouped_extra(pkg, flush, 20, 3, peak_tf, pk["hbm_gbs"])]
+                               run_grouped_extra(pkg, flush, 20, 3, peak_tf, pk["hbm_gbs"]),
+                               run_skinny_extra(pkg, flush, 30, 3, pk["hbm_gbs"]),
+                               run_quant_extra(pkg, flush, 30, 3, pk["hbm_gbs"])]
             line["gpu_launches_extras_note"] = "extras are separate timed loops, not part of gpu_launches"
     return line
 
