@@ -197,8 +197,8 @@ NVFP4_API int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, c
  * scales written straight into the 128x4 blocked layout (buffer of
  * ceil(M/128) * ceil(K/64) * 512 bytes; padding bytes are written as 0).
  * Per 16-element block, global scale 1.0:  s = e4m3_rne_satfinite(amax / 6),
- * q_i = e2m1_rne_satfinite(x_i / s) with IEEE f32 division; a block whose s is
- * 0 gets all-zero codes.  Finite inputs.  No counterpart in the reference
+ * q_i = e2m1_rne_satfinite(x_i * fl32(1 / s)) (one IEEE f32 reciprocal per
+ * block, f32 products); a block whose s is 0 gets all-zero codes.  Finite inputs.  No counterpart in the reference
  * (its inputs arrive already quantised); it produces the operands of
  * nvfp4_dual_gemm / nvfp4_grouped_gemm.
  */

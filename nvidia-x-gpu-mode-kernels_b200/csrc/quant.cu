@@ -5,9 +5,13 @@
 // Per 16-element block of a row (global scale 1.0):
 //   amax  = max |x_i|                                   (exact in f32)
 //   s     = e4m3(amax / 6)   round-to-nearest-even, saturating at 448
-//   q_i   = e2m1(x_i / s)    round-to-nearest-even, saturating at +-6
+//   inv   = 1 / s            one IEEE f32 division per block
+//   q_i   = e2m1(x_i * inv)  f32 product, then round-to-nearest-even,
+//                            saturating at +-6
 //   (s == 0, i.e. an all-zero or tiny block: every code is 0)
-// x_i / s is an IEEE f32 division, so the result is reproducible bit for bit.
+// Every step is a correctly rounded f32 operation, so the result is
+// reproducible bit for bit.  (An IEEE division per element made the kernel
+// compute-bound at 45 % of HBM bandwidth.)
 //
 // One thread per (row, block) position of the PADDED blocked scale matrix:
 // threads on padding rows / columns write a zero scale byte and nothing else,
@@ -39,19 +43,21 @@ __device__ __forceinline__ float e4m3_to_f32(uint32_t byte) {
   return lo;
 }
 
+// Index type I: 32-bit when every index fits (64-bit division is slow).
+template <typename I>
 __global__ void __launch_bounds__(256) quantize_kernel(const __half* __restrict__ x, int64_t M, int64_t K,
                                                        int64_t ldx, uint8_t* __restrict__ codes, int64_t ldq,
-                                                       uint8_t* __restrict__ sf, int64_t kbp, int64_t total) {
-  const int64_t kb = K / 16;
-  const int64_t nkt = kbp / 4;  // 4-block column tiles
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / kbp, c = i % kbp;   // consecutive threads: consecutive blocks of one row
-    const int64_t off = ((r / 128) * nkt + c / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4);
+                                                       uint8_t* __restrict__ sf, int64_t kbp_, int64_t total_) {
+  const I kb = (I)(K / 16), kbp = (I)kbp_, total = (I)total_;
+  const I nkt = kbp / 4;  // 4-block column tiles
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (I)gridDim.x * blockDim.x) {
+    const I r = i / kbp, c = i % kbp;   // consecutive threads: consecutive blocks of one row
+    const I off = ((r / 128) * nkt + c / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4);
     if (r >= M || c >= kb) {
       sf[off] = 0;
       continue;
     }
-    const __half* xp = x + r * ldx + c * 16;
+    const __half* xp = x + (int64_t)r * ldx + (int64_t)c * 16;
     float v[16];
     if ((reinterpret_cast<uintptr_t>(xp) & 15u) == 0) {
       const uint4 u0 = reinterpret_cast<const uint4*>(xp)[0];
@@ -74,13 +80,14 @@ __global__ void __launch_bounds__(256) quantize_kernel(const __half* __restrict_
     const float s = e4m3_to_f32(sbyte);
     uint32_t packed[2] = {0u, 0u};
     if (s > 0.f) {
+      const float inv = __fdiv_rn(1.0f, s);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const uint32_t b = e2m1x2_from_f32(__fdiv_rn(v[2 * j], s), __fdiv_rn(v[2 * j + 1], s));
+        const uint32_t b = e2m1x2_from_f32(__fmul_rn(v[2 * j], inv), __fmul_rn(v[2 * j + 1], inv));
         packed[j / 4] |= b << (8 * (j % 4));
       }
     }
-    uint8_t* qp = codes + r * ldq + c * 8;
+    uint8_t* qp = codes + (int64_t)r * ldq + (int64_t)c * 8;
     if ((reinterpret_cast<uintptr_t>(qp) & 7u) == 0) {
       *reinterpret_cast<uint2*>(qp) = make_uint2(packed[0], packed[1]);
     } else {
@@ -106,7 +113,9 @@ extern "C" int nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, 
   int64_t grid = (total + 255) / 256;
   const int64_t cap = (int64_t)sm_count() * 16;
   if (grid > cap) grid = cap;
-  quantize_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  // the largest index the kernel forms is the scale offset, below total + 512
+  auto kern = (total + 1024 < (int64_t)UINT32_MAX) ? quantize_kernel<uint32_t> : quantize_kernel<uint64_t>;
+  kern<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), M, K, ldx, static_cast<uint8_t*>(codes), ldq, static_cast<uint8_t*>(sf_blocked),
       kbp, total);
   return check_launch("quantize_kernel");

@@ -3,8 +3,8 @@
 ``quantize(x)`` returns ``(codes, scales_blocked)``: e2m1 codes [M, K/2]
 (uint8, two per byte, low nibble first) and e4m3 block-16 scales already in
 the 128x4 blocked layout that ``dual_gemm`` / ``grouped_gemm`` take.  Rules per
-16-element block (global scale 1.0): s = e4m3(amax / 6), q = e2m1(x / s), both
-round-to-nearest-even with saturation; an all-zero block quantises to zeros.
+16-element block (global scale 1.0): s = e4m3(amax / 6), q = e2m1(x * fl32(1/s)),
+both round-to-nearest-even with saturation; an all-zero block quantises to zeros.
 """
 from __future__ import annotations
 

@@ -274,7 +274,8 @@ def quantize(x) -> tuple[np.ndarray, np.ndarray]:
     sbyte = e4m3_rne_satfinite((amax / np.float32(6.0)).astype(np.float32).astype(np.float64))
     s = E4M3_LUT[sbyte].astype(np.float32)
     safe = np.where(s > 0, s, np.float32(1.0))
-    qv = (blocks / safe[:, :, None]).astype(np.float32)     # IEEE f32 division
+    inv = (np.float32(1.0) / safe).astype(np.float32)        # one IEEE f32 division per block
+    qv = (blocks * inv[:, :, None]).astype(np.float32)       # f32 product, correctly rounded
     codes = e2m1_rne_satfinite(qv.astype(np.float64))
     codes = np.where((s > 0)[:, :, None], codes, 0).astype(np.uint8).reshape(M, K)
     packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
