@@ -26,7 +26,6 @@
 //           thread), SiLU-gate or plain conversion to fp16, 16-byte stores.
 // Every mbarrier wait is bounded (2 s) and reports into the device error word.
 #include <cuda_fp16.h>
-#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include "ptx.cuh"
@@ -52,8 +51,6 @@ struct GemmGroup {
   int64_t ldc;                   // elements
   int M, N, K;
   int tiles_m, tiles_n, tile_begin;
-  int nks;                       // 256-element K steps per tile
-  int64_t unit_begin;            // stream-K: index of this group's first (tile, K step) unit
   int vec_ok;                    // c 16-byte aligned and ldc % 8 == 0: 16-byte stores
   int tma_store;                 // tc is valid: the epilogue stores through shared memory + TMA
 };
@@ -64,61 +61,6 @@ struct GemmParams {
   int ngroups;
   int total_tiles;
   uint32_t* err;
-  // stream-K (sk != 0): the (tile, K step) units are split evenly over the
-  // CTAs; a tile cut between CTAs c and c+1 is finished by c, which adds the
-  // fp32 partial that c+1 parked in work[c+1] (flagged by sk_flags[c+1] == epoch)
-  int sk;
-  uint32_t epoch;
-  int64_t total_units;
-  float* work;
-  uint32_t* sk_flags;
-};
-
-// One contiguous run of K steps of one tile, as a CTA walks its work.
-struct Seg {
-  int t, g, k0, k1;
-};
-
-// Whole tiles round-robin (sk == 0) or an even, contiguous share of the
-// (tile, K step) units (sk != 0).  Every warp role walks the same sequence.
-template <int MAXG>
-struct SegWalker {
-  int64_t u, u1;
-  int t;
-  __device__ explicit SegWalker(const GemmParams<MAXG>& P) {
-    if (P.sk) {
-      u = P.total_units * blockIdx.x / gridDim.x;
-      u1 = P.total_units * (blockIdx.x + 1) / gridDim.x;
-    } else {
-      t = blockIdx.x;
-    }
-  }
-  __device__ bool next(const GemmParams<MAXG>& P, Seg& s) {
-    if (!P.sk) {
-      if (t >= P.total_tiles) return false;
-      int g = 0;
-      while (g + 1 < P.ngroups && P.g[g + 1].tile_begin <= t) ++g;
-      s.t = t;
-      s.g = g;
-      s.k0 = 0;
-      s.k1 = P.g[g].nks;
-      t += gridDim.x;
-      return true;
-    }
-    if (u >= u1) return false;
-    int g = 0;
-    while (g + 1 < P.ngroups && P.g[g + 1].unit_begin <= u) ++g;
-    const GemmGroup& G = P.g[g];
-    const int64_t off = u - G.unit_begin;
-    const int local = (int)(off / G.nks);
-    s.t = G.tile_begin + local;
-    s.g = g;
-    s.k0 = (int)(off % G.nks);
-    const int64_t left = u1 - u;
-    s.k1 = (int)((G.nks - s.k0 < left) ? G.nks : s.k0 + left);
-    u += s.k1 - s.k0;
-    return true;
-  }
 };
 
 // DBG is a tuning knob (0 in every product instantiation): bit 0 skips the
@@ -278,14 +220,13 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       const uint64_t pol_a = policy_evict_last();   // A tiles are re-read by every N tile
       const uint64_t pol_b = C::POL ? policy_evict_normal() : policy_evict_first();
       uint32_t it = 0;
-      SegWalker<MAXG> W(P);
-      for (Seg sg; W.next(P, sg);) {
-        const int t = sg.t;
-        const GemmGroup& G = P.g[sg.g];
+      for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
+        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
         const int local = t - G.tile_begin;
         const int mt = local % G.tiles_m, nt = local / G.tiles_m;
         const int nk64 = G.K / 64;
-        for (int ks = sg.k0; ks < sg.k1; ++ks, ++it) {
+        const int nks = (nk64 + 3) / 4;
+        for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
           const uint32_t st = sbase + s * C::STAGE_BYTES;
@@ -328,17 +269,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     // ------------------------------ MMA -------------------------------
     if (lane == 0) {
       uint32_t it = 0, tile_it = 0;
-      SegWalker<MAXG> W(P);
-      for (Seg sg; W.next(P, sg); ++tile_it) {
-        const int t = sg.t;
-        const GemmGroup& G = P.g[sg.g];
+      for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
+        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
         const int nk64 = G.K / 64;
+        const int nks = (nk64 + 3) / 4;
         // a B tile narrower than 128 rows starts inside its scale block: its
         // scales begin (tile row offset / 32) columns into the block's 4
         const uint32_t sfb_off = (uint32_t)((((t - G.tile_begin) / G.tiles_m) * C::BN) % 128) / 32;
         if (!mbar_wait(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
         tc::fence_after_sync();
-        for (int ks = sg.k0; ks < sg.k1; ++ks, ++it) {
+        for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait((C::SFST ? bar_sfr : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull))
             goto done;
@@ -361,7 +301,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           const uint64_t da = tc::desc_sw128(st), db = tc::desc_sw128(st + C::OFF_B);
           const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
           for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
-            const uint32_t accum = (ks > sg.k0 || kk > 0) ? 1u : 0u;
+            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
             // the k-th 64-element slice starts 32 bytes further (encoded >> 4)
             tc::mma_mxf4nvf4(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk,
                              sfb_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
@@ -382,11 +322,11 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint32_t it = 0;
     bool dead = false;
-    SegWalker<MAXG> W(P);
-    for (Seg sg; W.next(P, sg);) {
-      const GemmGroup& G = P.g[sg.g];
+    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
+      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
       const int nk64 = G.K / 64;
-      for (int ks = sg.k0; ks < sg.k1; ++ks, ++it) {
+      const int nks = (nk64 + 3) / 4;
+      for (int ks = 0; ks < nks; ++ks, ++it) {
         const int s = it % C::STAGES;
         if (!dead && !mbar_wait((C::SEPSF ? bar_sff : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err,
                                 kDevErrTimeoutFull))
@@ -421,58 +361,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     const int sub = warp & 3;                 // tensor-memory lane quarter of this warp
     const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
     uint32_t tile_it = 0;
-    SegWalker<MAXG> W(P);
-    for (Seg sg; W.next(P, sg); ++tile_it) {
-      const int t = sg.t;
-      const GemmGroup& G = P.g[sg.g];
+    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
+      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
       const int local = t - G.tile_begin;
       const int mt = local % G.tiles_m, nt = local / G.tiles_m;
       if (!mbar_wait(bar_accf, tile_it & 1, P.err, kDevErrTimeoutMma)) break;
       tc::fence_after_sync();
       const int rloc = sub * 32 + lane;        // row of the tile held by this thread
       const int row = mt * BM + rloc;
-      // stream-K halves of a tile cut between this CTA and a neighbour
-      const bool sk_upper = P.sk && sg.k0 > 0;          // park the partial for CTA blockIdx.x - 1
-      const bool sk_lower = P.sk && sg.k1 < G.nks;      // add CTA blockIdx.x + 1's partial
-      if (sk_upper) {
-        float* slot = P.work + (size_t)blockIdx.x * C::ACC_COLS * BM;
-#pragma unroll 1
-        for (int cb = 0; cb < C::ACC_COLS / 32; ++cb) {
-          uint32_t v[32];
-          tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
-          tc::wait_ld();
-          if (cb == C::ACC_COLS / 32 - 1) {
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acce);
-          }
-#pragma unroll
-          for (int j = 0; j < 32; ++j) slot[(cb * 32 + j) * BM + rloc] = __uint_as_float(v[j]);   // column-major
-        }
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (threadIdx.x == 64) {
-          __threadfence();
-          asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(P.sk_flags + blockIdx.x), "r"(P.epoch) : "memory");
-        }
-        continue;
-      }
-      const float* peer = nullptr;
-      if (sk_lower) {
-        if (threadIdx.x == 64) {
-          const uint64_t t0 = globaltimer();
-          for (uint32_t i = 0;; ++i) {
-            uint32_t f;
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(f) : "l"(P.sk_flags + blockIdx.x + 1) : "memory");
-            if (f == P.epoch) break;
-            if ((i & 63u) == 63u && globaltimer() - t0 > kWaitBudgetNs) {
-              atomicOr(P.err, kDevErrTimeoutMma);
-              break;
-            }
-          }
-        }
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        peer = P.work + (size_t)(blockIdx.x + 1) * C::ACC_COLS * BM;
-      }
       if constexpr (C::TRANS) {
         // C^T: this thread's accumulator row is output column `row`; its BN
         // columns are tokens.  A warp stores 32 consecutive output columns of
@@ -514,13 +410,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           uint32_t u[32];
           tc::ld_32x32b_x32(tmem + lane_base + C::BN + cb * 32, u);
           tc::wait_ld();
-          if (peer) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              v[j] = __float_as_uint(__uint_as_float(v[j]) + peer[(cb * 32 + j) * BM + rloc]);
-              u[j] = __float_as_uint(__uint_as_float(u[j]) + peer[(C::BN + cb * 32 + j) * BM + rloc]);
-            }
-          }
           if (cb == C::BN / 32 - 1) {   // accumulator fully read: let the next tile's MMAs start
             tc::fence_before_sync();
             __syncwarp();
@@ -532,10 +421,6 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
                            silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
         } else {
           tc::wait_ld();
-          if (peer) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + peer[(cb * 32 + j) * BM + rloc]);
-          }
           if (cb == C::BN / 32 - 1) {
             tc::fence_before_sync();
             __syncwarp();
@@ -896,8 +781,8 @@ int launch_gemm(const GemmParams<MAXG>& P, cudaStream_t stream) {
     attr_set[dev] = true;
   }
   int grid = sm_count();
-  if (!P.sk && P.total_tiles < grid) grid = P.total_tiles;
-  if (grid < 1 || P.total_tiles < 1) return NVFP4_OK;
+  if (P.total_tiles < grid) grid = P.total_tiles;
+  if (grid < 1) return NVFP4_OK;
   gemm_kernel<C, MAXG><<<grid, C::THREADS, C::SMEM, stream>>>(P);
   return check_launch("gemm_kernel");
 }
@@ -938,70 +823,6 @@ int launch_gemm2(const GemmParams<MAXG>& P, cudaStream_t stream) {
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm2)");
   return check_launch("gemm2_kernel");
-}
-
-// Stream-K set-up for a single-CTA launch: on when the tiles do not divide
-// evenly over the SMs (a partial last wave) and every CTA gets at least one
-// whole tile of K steps (so a tile is cut at most once).  The fp32 workspace
-// (one accumulator image per CTA) and the per-CTA flags are allocated once per
-// device and grown when needed; flags carry a running epoch, so they are never
-// cleared between launches.  Launches that use stream-K must not overlap on the
-// GPU (they share the workspace).  NVFP4_GEMM_STREAMK=0 turns it off.
-struct SkState {
-  float* work = nullptr;
-  uint32_t* flags = nullptr;
-  size_t work_floats = 0;
-  int flag_words = 0;
-  uint32_t epoch = 0;
-};
-SkState g_sk[64];
-std::mutex g_sk_mu;
-
-template <class C, int MAXG>
-int streamk_setup(GemmParams<MAXG>& P) {
-  P.sk = 0;
-  static const bool enabled = [] {
-    const char* e = getenv("NVFP4_GEMM_STREAMK");
-    return !(e && e[0] == '0');
-  }();
-  if (!enabled || C::PAIR || C::EPI || C::TRANS) return NVFP4_OK;
-  const int grid = sm_count();
-  int max_nks = 0;
-  int64_t units = 0;
-  for (int i = 0; i < P.ngroups; ++i) {
-    P.g[i].unit_begin = units;
-    units += (int64_t)P.g[i].tiles_m * P.g[i].tiles_n * P.g[i].nks;
-    if (P.g[i].nks > max_nks) max_nks = P.g[i].nks;
-  }
-  P.total_units = units;
-  if (P.total_tiles % grid == 0 || units < (int64_t)grid * max_nks) return NVFP4_OK;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return NVFP4_OK;
-  std::lock_guard<std::mutex> lk(g_sk_mu);
-  SkState& S = g_sk[dev];
-  const size_t need = (size_t)grid * C::ACC_COLS * BM;
-  if (S.work_floats < need || S.flag_words < grid) {
-    if (S.work) cudaFree(S.work);
-    if (S.flags) cudaFree(S.flags);
-    S.work = nullptr;
-    S.flags = nullptr;
-    S.work_floats = 0;
-    S.flag_words = 0;
-    cudaError_t e = cudaMalloc(&S.work, need * sizeof(float));
-    if (e == cudaSuccess) e = cudaMalloc(&S.flags, (size_t)grid * sizeof(uint32_t));
-    if (e == cudaSuccess) e = cudaMemset(S.flags, 0, (size_t)grid * sizeof(uint32_t));
-    if (e != cudaSuccess) return cuda_fail(e, "stream-K workspace");
-    S.work_floats = need;
-    S.flag_words = grid;
-    S.epoch = 0;
-  }
-  P.sk = 1;
-  P.epoch = ++S.epoch;
-  if (P.epoch == 0) P.epoch = ++S.epoch;   // 0 is the flags' initial value
-  P.work = S.work;
-  P.sk_flags = S.flags;
-  return NVFP4_OK;
 }
 
 template <class C, int MAXG>
@@ -1088,13 +909,11 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   G.M = (int)M; G.N = (int)N; G.K = (int)K;
   G.tiles_m = (int)((M + C::TILE_M - 1) / C::TILE_M);
   G.tiles_n = (int)((N + C::BN - 1) / C::BN);
-  G.nks = (int)((K / 64 + 3) / 4);
   G.tile_begin = 0;
   P.ngroups = 1;
   P.total_tiles = G.tiles_m * G.tiles_n;
   P.err = device_error_word();
   if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_dual_gemm: cannot resolve the device error word");
-  if ((rc = streamk_setup<C, 1>(P))) return rc;
   return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
@@ -1132,7 +951,6 @@ int skinny_run(const void* x, const void* w, const void* sfx, const void* sfw, v
   G.K = (int)K;
   G.tiles_m = (int)((N + BM - 1) / BM);
   G.tiles_n = 1;
-  G.nks = (int)((K / 64 + 3) / 4);
   P.ngroups = 1;
   P.total_tiles = G.tiles_m;
   P.err = device_error_word();
@@ -1174,7 +992,6 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
       G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
       G.tiles_m = (int)((q.M + C::TILE_M - 1) / C::TILE_M);
       G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
-      G.nks = (int)((q.K / 64 + 3) / 4);
       G.tile_begin = tiles;
       tiles += G.tiles_m * G.tiles_n;
       ++n;
@@ -1183,9 +1000,7 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
     P.ngroups = n;
     P.total_tiles = tiles;
     P.err = err;
-    int rc = streamk_setup<C, MAXG>(P);
-    if (rc) return rc;
-    rc = launch_any<C, MAXG>(P, static_cast<cudaStream_t>(stream));
+    int rc = launch_any<C, MAXG>(P, static_cast<cudaStream_t>(stream));
     if (rc) return rc;
   }
   return NVFP4_OK;
