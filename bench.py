@@ -545,7 +545,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--profile", nargs="?", const="gemv", default=None, choices=["gemv", "dual", "grouped"],
+    ap.add_argument("--profile", nargs="?", const="gemv", default=None, choices=["gemv", "gemv2", "dual", "grouped", "skinny", "quant"],
                     help="run only one kernel (warmup + steps launches) for ncu captures")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -559,6 +559,14 @@ def main():
             x = pkg.inputs.gemv_inputs(HEADLINE["M"], HEADLINE["K"], HEADLINE["L"], seed=0, device="cuda")
             for _ in range(args.warmup + args.steps):
                 pkg.custom_kernel(*x.as_tuple())
+        elif args.profile == "gemv2":
+            x = pkg.inputs.gemv_inputs(4096, 14336, 8, seed=0, device="cuda")
+            for _ in range(args.warmup + args.steps):
+                pkg.custom_kernel(*x.as_tuple())
+        elif args.profile == "skinny":
+            run_skinny_extra(pkg, noflush, args.steps, args.warmup, 1.0)
+        elif args.profile == "quant":
+            run_quant_extra(pkg, noflush, args.steps, args.warmup, 1.0)
         elif args.profile == "dual":
             run_dual_extra(pkg, noflush, args.steps, args.warmup, 1.0, 1.0)
         else:
