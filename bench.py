@@ -251,16 +251,18 @@ def run_gemv_extra(pkg, flush, M, K, L, steps, warmup):
             "us_median": round(statistics.median(ts) * 1e3, 3)}
 
 
-def fp4_peak_tflops(pkg, iters=4096, reps=5):
-    """Dense FP4 tensor throughput measured with the library's MMA probe."""
+def fp4_peak_tflops(pkg, iters=4096, reps=5, pattern=0):
+    """Dense FP4 tensor throughput measured with the library's MMA probe.
+    pattern 0: fixed scale columns (the GEMM fractions' denominator); 1: the
+    GEMMs' operand and scale-column pattern (random bytes, per-K-step scales)."""
     lib = pkg._lib.lib()
     stream = torch.cuda.current_stream().cuda_stream
-    pkg._lib.check(lib.nvfp4_mma_peak(iters, stream))
+    pkg._lib.check(lib.nvfp4_mma_peak_pattern(iters, pattern, stream))
     ts = []
     for _ in range(reps):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        pkg._lib.check(lib.nvfp4_mma_peak(iters, stream))
+        pkg._lib.check(lib.nvfp4_mma_peak_pattern(iters, pattern, stream))
         e1.record()
         torch.cuda.synchronize()
         ts.append(e0.elapsed_time(e1))
@@ -468,6 +470,7 @@ def our_arm(args, world, rank, local):
                 e["hbm_frac"] = round(e["gbs"] / pk["hbm_gbs"], 4)
             peak_tf = fp4_peak_tflops(pkg)
             line["fp4_peak_tflops_measured"] = round(peak_tf, 1)
+            line["fp4_peak_tflops_gemm_pattern"] = round(fp4_peak_tflops(pkg, pattern=1), 1)
             line["extras"] += [run_dual_extra(pkg, flush, 30, 3, peak_tf, pk["hbm_gbs"]),
                                run_grouped_extra(pkg, flush, 20, 3, peak_tf, pk["hbm_gbs"]),
                                run_skinny_extra(pkg, flush, 30, 3, pk["hbm_gbs"]),

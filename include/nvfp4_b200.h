@@ -213,6 +213,16 @@ NVFP4_API int nvfp4_quantize(const void* x, int64_t M, int64_t K, int64_t ldx, v
  */
 NVFP4_API int nvfp4_mma_peak(int iters, void* stream);
 
+/*
+ * The same probe under a chosen operand pattern: 0 = one fixed scale column
+ * pair and whatever shared memory holds (what nvfp4_mma_peak runs); 1 = the
+ * GEMMs' conditions: pseudo-random operand bytes, e4m3 scales in 2^[-3, 3],
+ * scale columns advancing per K step through four 48-column stages.  The
+ * tensor pipe's rate depends on both, so pattern 1 is the attainable rate for
+ * the GEMM kernels' instruction stream.
+ */
+NVFP4_API int nvfp4_mma_peak_pattern(int iters, int pattern, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

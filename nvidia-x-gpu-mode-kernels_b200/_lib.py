@@ -36,6 +36,7 @@ SIGNATURES: dict[str, list] = {
     "nvfp4_dual_gemm": [VP, VP, VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_grouped_gemm": [ctypes.POINTER(Group), ctypes.c_int, VP],
     "nvfp4_mma_peak": [ctypes.c_int, VP],
+    "nvfp4_mma_peak_pattern": [ctypes.c_int, ctypes.c_int, VP],
     "nvfp4_quantize": [VP, I64, I64, I64, VP, I64, VP, VP],
     "nvfp4_gemm_skinny": [VP, VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, VP],
     "nvfp4_gemv_grid": [I64, I64, I64, ctypes.POINTER(I64)],

@@ -77,9 +77,10 @@ struct GemmParams {
 // TRANS 1 (skinny GEMM): A holds weight rows, B the token rows, and the
 // epilogue writes C^T, i.e. out[token][weight row]; one N tile only.
 template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1,
-          int SEPSF_ = 1, int TRANS_ = 0>
+          int SEPSF_ = 1, int TRANS_ = 0, int PB_ = 1>
 struct GemmCfg {
   static constexpr int TRANS = TRANS_;
+  static constexpr int PB = PB_;         // producer refills the ring PB stages at a time
   static constexpr int SFTMA = SFTMA_;   // scales by tensor-map TMA (1) or 1-D bulk copies (0)
   static constexpr int SEPSF = (SEPSF_ && SFST_ && SFTMA_) ? 1 : 0;
   static constexpr int DBG = DBG_;
@@ -236,7 +237,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int nks = (nk64 + 3) / 4;
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
-          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
+          if (C::PB == 1) {
+            if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
+          } else if (it % C::PB == 0) {
+            // wait until the next PB slots are all free, then fill them back to back
+            for (uint32_t j = it; j < it + C::PB; ++j)
+              if (!mbar_wait(bar_empty + 8 * (j % C::STAGES), ((j / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty))
+                goto done;
+          }
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const uint32_t fb = bar_full + 8 * s;
           const int nch = min(4, nk64 - 4 * ks);
@@ -1078,7 +1086,13 @@ extern "C" int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, 
 // ---------------------------------------------------------------------------
 namespace nvfp4 {
 namespace {
-__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, uint32_t* err) {
+// Dense FP4 throughput probe: back-to-back 128x256x64 kind::mxf4nvf4 MMAs
+// on every SM.  pattern 0: one fixed scale column pair and whatever shared
+// memory holds.  pattern 1 (the GEMMs' conditions): pseudo-random operand
+// bytes, e4m3 scales in 2^[-3, 3], and the scale columns advancing per K
+// step through four 48-column stages exactly as the GEMM's tensor-memory
+// layout does.  The tensor pipe's rate depends on both.
+__global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, int pattern, uint32_t* err) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
@@ -1097,11 +1111,35 @@ __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, uint32_t* e
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem_raw + (slot - raw));
+  if (pattern == 1) {
+    uint32_t* ops = reinterpret_cast<uint32_t*>(smem_raw + (sbase - raw));
+    for (int i = threadIdx.x; i < 49152 / 4; i += blockDim.x) {
+      uint32_t x = (uint32_t)i * 2654435761u ^ (blockIdx.x * 40503u);
+      x ^= x >> 15; x *= 0x2c1b3c6du; x ^= x >> 12;
+      ops[i] = x;
+    }
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    for (int c = 256; c < 256 + 4 * 48; c += 2) {   // each warp: its 32-lane quarter, two columns per store
+      const uint32_t x = (uint32_t)(c * 131 + (threadIdx.x & 31) * 7 + blockIdx.x);
+      uint32_t v = 0;
+      for (int b = 0; b < 4; ++b) v |= (((x >> (3 * b)) % 7u) + 4u) << 3 << (8 * b);   // bytes 0x20..0x50: 2^-3 .. 2^3
+      tc::st_32x32b_x2(tmem + lane_base + c, v, v ^ 0x08080808u);
+    }
+    tc::wait_st();
+    fence_proxy_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+  }
   if (threadIdx.x == 0) {
     const uint64_t da = tc::desc_sw128(sbase), db = tc::desc_sw128(sbase + 16384);
     const uint32_t idesc = tc::idesc_mxf4nvf4(128, 256);
-    for (int i = 0; i < iters; ++i)
-      tc::mma_mxf4nvf4(tmem, da + 2 * (i & 3), db + 2 * (i & 3), idesc, tmem + 256, tmem + 272, i > 0 ? 1u : 0u);
+    for (int i = 0; i < iters; ++i) {
+      const int k = i & 3;
+      const uint32_t st = 256u + 48u * (uint32_t)((i >> 2) & 3);
+      const uint32_t sfa = pattern ? st + 4 * k : 256u, sfb = pattern ? st + 16 + 8 * k : 272u;
+      tc::mma_mxf4nvf4(tmem, da + 2 * k, db + 2 * k, idesc, tmem + sfa, tmem + sfb, i > 0 ? 1u : 0u);
+    }
     tc::commit(bar);
     mbar_wait(bar, 0, err, kDevErrTimeoutMma);
   }
@@ -1115,8 +1153,9 @@ __global__ void __launch_bounds__(128, 1) mma_peak_kernel(int iters, uint32_t* e
 }  // namespace
 }  // namespace nvfp4
 
-extern "C" int nvfp4_mma_peak(int iters, void* stream) {
+extern "C" int nvfp4_mma_peak_pattern(int iters, int pattern, void* stream) {
   if (iters < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_mma_peak: iters must be positive");
+  if (pattern != 0 && pattern != 1) return fail(NVFP4_ERR_INVALID, "nvfp4_mma_peak_pattern: pattern must be 0 or 1");
   uint32_t* err = device_error_word();
   if (!err) return fail(NVFP4_ERR_CUDA, "nvfp4_mma_peak: cannot resolve the device error word");
   constexpr int kSmem = 49152 + 64 + 1024;
@@ -1128,6 +1167,8 @@ extern "C" int nvfp4_mma_peak(int iters, void* stream) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mma_peak)");
     attr_set[dev] = true;
   }
-  mma_peak_kernel<<<sm_count(), 128, kSmem, static_cast<cudaStream_t>(stream)>>>(iters, err);
+  mma_peak_kernel<<<sm_count(), 128, kSmem, static_cast<cudaStream_t>(stream)>>>(iters, pattern, err);
   return check_launch("mma_peak_kernel");
 }
+
+extern "C" int nvfp4_mma_peak(int iters, void* stream) { return nvfp4_mma_peak_pattern(iters, 0, stream); }

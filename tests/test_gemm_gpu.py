@@ -104,8 +104,11 @@ def test_plain_scales_are_converted(pkg, oracle, cuda):
 def test_mma_peak_probe_runs(pkg, cuda):
     s = torch.cuda.current_stream().cuda_stream
     pkg._lib.check(pkg._lib.lib().nvfp4_mma_peak(64, s))
+    pkg._lib.check(pkg._lib.lib().nvfp4_mma_peak_pattern(64, 1, s))
     torch.cuda.synchronize()
     assert pkg._lib.device_errors() == 0
+    with pytest.raises(RuntimeError, match="pattern"):
+        pkg._lib.check(pkg._lib.lib().nvfp4_mma_peak_pattern(64, 2, s))
 
 
 @pytest.mark.parametrize("T,N,K", [(1, 4096, 4096), (8, 14336, 4096), (16, 1000, 512), (17, 640, 256), (64, 256, 1024),
