@@ -532,15 +532,22 @@ int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullpt
   const int64_t kb = p.K / 2;
   const int64_t rows = p.M * p.L;
   const int64_t sms = sm_count();
-  if (rows < sms * 16) {
-    if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
-    return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
-  }
   // widest row slice whose last stage is not mostly padding: K/2 = 7168
   // bytes is 3.5 slices of 2 KB (a half-empty last stage per tile, 52.3 us on
   // config 2) but exactly 7 slices of 1 KB (48.6 us)
   auto pad = [kb](int64_t w) { return ((kb + w - 1) / w) * w - kb; };
-  if (kb >= 2048 && pad(2048) <= pad(1024)) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
+  const bool wide = kb >= 2048 && pad(2048) <= pad(1024);
+  if (rows < sms * 16) {
+    // fewer than 16 rows per SM (the per-rank share of a row-sharded GEMV at
+    // 8 GPUs): 4-row tiles, four CTAs per SM (M=2048, K=16384: 11.5 vs 12.0 us)
+    if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
+    if (wide) return launch_tma<GemvCfg<4, 2048, 4, 4, 4>>(p, st, grid_out);
+    return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
+  }
+  // fewer than two 16-row tiles per SM: two CTAs per SM spread them over
+  // twice the CTAs (M=4096, K=16384: 14.9 vs 16.1 us)
+  if (rows < sms * 32 && kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
+  if (wide) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
   if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
   return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st, grid_out);
 }

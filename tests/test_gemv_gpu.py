@@ -45,6 +45,10 @@ def _check(oracle, got, a, b, sfa, sfb, M, K, L, strict=True):
     (33, 1040, 2),      # K % 256 != 0 -> plain-load path
     (7, 48, 5),
     (512, 16384, 1),
+    (2048, 16384, 1),   # < 16 rows per SM, wide stages (the 8-rank share of config 1)
+    (1000, 6144, 1),    # < 16 rows per SM, K/2 = 3072: 1 KB stages
+    (4096, 16384, 1),   # < 32 rows per SM: two CTAs per SM (the 4-rank share of config 1)
+    (3000, 8192, 1),    # same class, ragged last tile
 ])
 def test_gemv_parity(pkg, oracle, cuda, M, K, L):
     x = pkg.inputs.gemv_inputs(M, K, L, seed=M + K + L, device=cuda)
