@@ -69,6 +69,32 @@ def test_quantize_strided_input(pkg, oracle, cuda):
 
 
 @pytest.mark.gpu
+def test_quantize_odd_alignment(pkg, oracle, cuda):
+    """A row stride and base offset that are odd in elements: 2-byte aligned input rows."""
+    g = torch.Generator().manual_seed(13)
+    big = torch.randn((40, 1043), generator=g).to(torch.float16)
+    x = big[:, 1:1025]                    # base offset 2 bytes, row stride 1043 elements
+    codes, sf = pkg.quantize(big.to(cuda)[:, 1:1025])
+    torch.cuda.synchronize()
+    rc, rs = oracle.quantize(x.numpy())
+    np.testing.assert_array_equal(codes.cpu().numpy(), rc)
+    np.testing.assert_array_equal(sf.cpu().numpy(), rs)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,K", [(129, 16400), (3, 32784)])
+def test_quantize_long_rows(pkg, oracle, cuda, M, K):
+    """Rows longer than one CTA's 1024 blocks (the threads loop over the row)."""
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn((M, K), generator=g).to(torch.float16)
+    codes, sf = pkg.quantize(x.to(cuda))
+    torch.cuda.synchronize()
+    rc, rs = oracle.quantize(x.numpy())
+    np.testing.assert_array_equal(codes.cpu().numpy(), rc)
+    np.testing.assert_array_equal(sf.cpu().numpy(), rs)
+
+
+@pytest.mark.gpu
 def test_quantize_then_dual_gemm(pkg, oracle, cuda):
     M, N, K = 256, 1024, 1024
     g = torch.Generator().manual_seed(11)
