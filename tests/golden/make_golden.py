@@ -2,7 +2,7 @@
 kernel (blackwell_nvfp4_gemv.cu, built from its own source into oracle/_ref by
 oracle/build_ref.py) on a GPU.
 
-    python tests/golden/make_golden.py <out_dir>
+    python tests/golden/make_golden.py [out_dir]     (default: next to this script)
 
 Fixtures (npz, inputs included so the CPU tests need no generator):
   kat_e2m1.npz  M=32 K=512 L=16: row m's first 16-element block holds code m%16,
@@ -74,4 +74,4 @@ def main(out):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else os.path.join(ROOT, "gpurun_out", "golden"))
+    main(sys.argv[1] if len(sys.argv) > 1 else os.path.dirname(os.path.abspath(__file__)))
