@@ -545,8 +545,11 @@ int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullpt
     return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
   }
   // fewer than two 16-row tiles per SM: two CTAs per SM spread them over
-  // twice the CTAs (M=4096, K=16384: 14.9 vs 16.1 us)
-  if (rows < sms * 32 && kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
+  // twice the CTAs (M=4096, K=16384: 14.9 vs 16.1 us).  Not with the fused
+  // all-gather, whose completion costs a system fence and a count per CTA:
+  // there the 296-CTA grid made the 4-rank step slower (35.2 vs 34.0 us for
+  // kernel + NCCL).
+  if (rows < sms * 32 && kb >= 1024 && p.world == 0) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
   if (wide) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
   if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
   return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st, grid_out);
