@@ -77,10 +77,9 @@ struct GemmParams {
 // TRANS 1 (skinny GEMM): A holds weight rows, B the token rows, and the
 // epilogue writes C^T, i.e. out[token][weight row]; one N tile only.
 template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1,
-          int SEPSF_ = 1, int TRANS_ = 0, int PB_ = 1, int KA_ = 1>
+          int SEPSF_ = 1, int TRANS_ = 0, int KA_ = 1>
 struct GemmCfg {
   static constexpr int TRANS = TRANS_;
-  static constexpr int PB = PB_;         // producer refills the ring PB stages at a time
   // KA 128-byte K atoms (256 elements each) per stage: one TMA box per atom and
   // operand, 4 * KA MMAs per stage, scale boxes of 4 * KA K-blocks
   static constexpr int KA = KA_;
@@ -246,14 +245,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         const int nks = (nk64 + C::KPS - 1) / C::KPS;
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
-          if (C::PB == 1) {
-            if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
-          } else if (it % C::PB == 0) {
-            // wait until the next PB slots are all free, then fill them back to back
-            for (uint32_t j = it; j < it + C::PB; ++j)
-              if (!mbar_wait(bar_empty + 8 * (j % C::STAGES), ((j / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty))
-                goto done;
-          }
+          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const uint32_t fb = bar_full + 8 * s;
           // scale boxes always count in full (blocks past the end read as zeros)
@@ -997,7 +989,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
                                int64_t ldb, int64_t ldc, void* stream) {
   // two 512-element K stages of 108 KB: half the stage handshakes of four 256-element
   // stages at the same bytes in flight (30.9 vs 33.3 us on the dual workload, same box)
-  return dual_run<GemmCfg<128, true, 2, 0, 1, 0, 0, 1, 1, 0, 1, 2>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb,
+  return dual_run<GemmCfg<128, true, 2, 0, 1, 0, 0, 1, 1, 0, 2>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb,
                                                                    ldc, stream);
 }
 
@@ -1095,10 +1087,10 @@ extern "C" int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, 
   // 512-element K stages (32 KB of weights each): half the per-stage handshakes of
   // 256-element stages (13.8 vs 16.3 us at T=16, N=14336, K=4096)
   if (T <= 16)
-    return skinny_run<GemmCfg<16, false, 4, 0, 1, 0, 0, 1, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+    return skinny_run<GemmCfg<16, false, 4, 0, 1, 0, 0, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
   if (T <= 32)
-    return skinny_run<GemmCfg<32, false, 4, 0, 1, 0, 0, 1, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
-  return skinny_run<GemmCfg<64, false, 4, 0, 1, 0, 0, 1, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+    return skinny_run<GemmCfg<32, false, 4, 0, 1, 0, 0, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+  return skinny_run<GemmCfg<64, false, 4, 0, 1, 0, 0, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
 }
 
 // ---------------------------------------------------------------------------
