@@ -251,6 +251,30 @@ def run_gemv_extra(pkg, flush, M, K, L, steps, warmup):
             "us_median": round(statistics.median(ts) * 1e3, 3)}
 
 
+def run_gemv_b2b_extra(pkg, M, K, L, launches=20, reps=5):
+    """Steady-state throughput: `launches` back-to-back launches between one
+    event pair, no flush between them.  Valid only because the inputs are larger
+    than L2 (config 1: 151 MB against 126 MB, A streamed with an evict-first
+    policy), so every launch reads its operands from DRAM again; the ncu launch
+    list of `--profile gemv` (no cache control) shows the DRAM bytes per launch."""
+    x = pkg.inputs.gemv_inputs(M, K, L, seed=0, device="cuda")
+    for _ in range(3):
+        pkg.custom_kernel(*x.as_tuple())
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(launches):
+            pkg.custom_kernel(*x.as_tuple())
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e3 / launches)
+    us = statistics.mean(ts)
+    return {"workload": f"gemv M={M} K={K} L={L}, {launches} back-to-back launches (inputs > L2, no flush)",
+            "us": round(us, 3), "gbs": round(x.nbytes_algorithmic() / (us * 1e-6) / 1e9, 1)}
+
+
 def fp4_peak_tflops(pkg, iters=4096, reps=5, pattern=0):
     """Dense FP4 tensor throughput measured with the library's MMA probe.
     pattern 0: fixed scale columns (the GEMM fractions' denominator); 1: the
@@ -465,7 +489,8 @@ def our_arm(args, world, rank, local):
                                 "sample": sample, "host_cpus": os.cpu_count()}
         if not args.no_extras:
             line["extras"] = [run_gemv_extra(pkg, flush, 256, 1024, 1, 50, 5),
-                              run_gemv_extra(pkg, flush, 4096, 14336, 8, 20, 3)]
+                              run_gemv_extra(pkg, flush, 4096, 14336, 8, 20, 3),
+                              run_gemv_b2b_extra(pkg, M, K, L)]
             for e in line["extras"]:
                 e["hbm_frac"] = round(e["gbs"] / pk["hbm_gbs"], 4)
             peak_tf = fp4_peak_tflops(pkg)
