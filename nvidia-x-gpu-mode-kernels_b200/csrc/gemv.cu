@@ -539,9 +539,11 @@ int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullpt
   const bool wide = kb >= 2048 && pad(2048) <= pad(1024);
   if (rows < sms * 16) {
     // fewer than 16 rows per SM (the per-rank share of a row-sharded GEMV at
-    // 8 GPUs): 4-row tiles, four CTAs per SM (M=2048, K=16384: 11.5 vs 12.0 us)
+    // 8 GPUs): 4-row tiles, four CTAs per SM (M=2048, K=16384: 11.5 vs 12.0 us
+    // with 2 KB stages; the fused all-gather keeps the 1 KB-stage form it was
+    // measured with at 8 ranks)
     if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
-    if (wide) return launch_tma<GemvCfg<4, 2048, 4, 4, 4>>(p, st, grid_out);
+    if (wide && p.world == 0) return launch_tma<GemvCfg<4, 2048, 4, 4, 4>>(p, st, grid_out);
     return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
   }
   // fewer than two 16-row tiles per SM: two CTAs per SM spread them over
