@@ -50,3 +50,43 @@ def test_gemv_rejects_bad_shapes_without_gpu(pkg):
     assert rc == 1 and b"null" in l.nvfp4_last_error()
     with pytest.raises(RuntimeError, match="INVALID"):
         pkg._lib.check(rc)
+
+
+def test_gemm_entry_points_reject_bad_arguments_without_gpu(pkg):
+    """Every GEMM-side entry point validates its arguments before any CUDA call."""
+    l = pkg._lib.lib()
+    msg = lambda: l.nvfp4_last_error()
+    p = 4096   # a 16-byte-aligned stand-in address: validation never dereferences it
+    # skinny GEMM: token count, K granularity, null operand
+    assert l.nvfp4_gemm_skinny(p, p, p, p, p, 0, 128, 256, 128, 128, 128, None) == 1 and b"1..64" in msg()
+    assert l.nvfp4_gemm_skinny(p, p, p, p, p, 65, 128, 256, 128, 128, 128, None) == 1 and b"1..64" in msg()
+    assert l.nvfp4_gemm_skinny(p, p, p, p, p, 8, 128, 96, 48, 48, 128, None) == 1 and b"multiple of 64" in msg()
+    assert l.nvfp4_gemm_skinny(None, p, p, p, p, 8, 128, 256, 128, 128, 128, None) == 1 and b"null" in msg()
+    # dual GEMM: K granularity, row stride below K/2, misaligned operand
+    assert l.nvfp4_dual_gemm(p, p, p, p, p, p, p, 128, 128, 100, 64, 64, 128, None) == 1
+    assert l.nvfp4_dual_gemm(p, p, p, p, p, p, p, 128, 128, 256, 64, 128, 128, None) == 1 and b"stride" in msg()
+    assert l.nvfp4_dual_gemm(p + 8, p, p, p, p, p, p, 128, 128, 256, 128, 128, 128, None) == 2
+    # grouped GEMM: no groups
+    assert l.nvfp4_grouped_gemm(None, 0, None) == 1 and b"no groups" in msg()
+    # quantiser: K granularity, odd fp16 address, misaligned scale buffer
+    assert l.nvfp4_quantize(p, 8, 24, 24, p, 12, p, None) == 1
+    assert l.nvfp4_quantize(p + 1, 8, 32, 32, p, 16, p, None) == 2
+    assert l.nvfp4_quantize(p, 8, 32, 32, p, 16, p + 2, None) == 2 and b"4-byte" in msg()
+    # tensor-core probe: iteration count and pattern
+    assert l.nvfp4_mma_peak_pattern(0, 0, None) == 1
+    assert l.nvfp4_mma_peak_pattern(16, 7, None) == 1 and b"pattern" in msg()
+
+
+def test_allgather_rejects_bad_world_without_gpu(pkg):
+    l = pkg._lib.lib()
+    outs = (ctypes.c_void_p * 8)(*([4096] * 8))
+    flags = (ctypes.c_void_p * 8)(*([4096] * 8))
+    args = lambda world, rank: (4096, 4096, 4096, 4096, 64, 512, 1, 256, 0, 0, 32, 0, 0,
+                                ctypes.cast(outs, ctypes.c_void_p), 1, 0, 0, ctypes.cast(flags, ctypes.c_void_p),
+                                world, rank, 1, None)
+    assert l.nvfp4_gemv_allgather(*args(9, 0)) == 1 and b"world" in l.nvfp4_last_error()
+    assert l.nvfp4_gemv_allgather(*args(2, 2)) == 1
+    nulls = (ctypes.c_void_p * 8)()
+    a = list(args(2, 0))
+    a[13] = ctypes.cast(nulls, ctypes.c_void_p)
+    assert l.nvfp4_gemv_allgather(*a) == 1 and b"null peer" in l.nvfp4_last_error()
