@@ -560,23 +560,28 @@ done:
 //     scale warps and the epilogue warps of each CTA meet at a named barrier
 //     and send one arrival per CTA to the leader (`sf_ready`, `acce`).
 // ===========================================================================
-template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFTMA_ = 1>
+template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFTMA_ = 1, int KA_ = 1>
 struct Gemm2Cfg {
+  static constexpr int KA = KA_;                           // 128-byte K atoms per stage (as in GemmCfg)
   static constexpr int SFTMA = SFTMA_;
   static constexpr int DBG = DBG_;                         // tuning knob as in GemmCfg (0 in the product)
   static constexpr int BN = BN_;                           // N per pair MMA (per B operand)
   static constexpr bool DUAL = DUAL_;
   static constexpr int STAGES = STAGES_;
   static constexpr int HB = BN / 2;                        // B rows per CTA
-  static constexpr int KPS = 4;                            // 64-element K blocks per stage
+  static constexpr int KPS = 4 * KA_;                      // 64-element K blocks per stage
   static constexpr int NB = (BN + 127) / 128;              // 128-row scale blocks of B per tile
-  static constexpr int A_BYTES = BM * KSTEP_BYTES;
-  static constexpr int B_BYTES = HB * KSTEP_BYTES;
+  static constexpr int A_ATOM = BM * KSTEP_BYTES;
+  static constexpr int B_ATOM = HB * KSTEP_BYTES;
+  static constexpr int A_BYTES = KA * A_ATOM;
+  static constexpr int B_BYTES = KA * B_ATOM;
   static constexpr int OFF_B = A_BYTES;
   static constexpr int OFF_B2 = OFF_B + B_BYTES;
   static constexpr int OFF_SFA = OFF_B2 + (DUAL ? B_BYTES : 0);
-  static constexpr int OFF_SFB = OFF_SFA + 2048;
-  static constexpr int SFB_BYTES = NB * 2048;
+  static constexpr int SFA_BYTES = KPS * 512;
+  static constexpr int SFB_ROWTILE = KPS * 512;
+  static constexpr int OFF_SFB = OFF_SFA + SFA_BYTES;
+  static constexpr int SFB_BYTES = NB * SFB_ROWTILE;
   static constexpr int OFF_SFB2 = OFF_SFB + SFB_BYTES;
   static constexpr int STAGE_BYTES = ((OFF_SFB2 + (DUAL ? SFB_BYTES : 0)) + 1023) / 1024 * 1024;
   static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
@@ -585,7 +590,8 @@ struct Gemm2Cfg {
   static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
   static constexpr int SF_BASE = ACC_COLS;
   static constexpr int SFBC = NB * 4;                      // B-scale columns per 64-element K block
-  static constexpr int SF_STAGE_COLS = 16 + 4 * SFBC * (DUAL ? 2 : 1);
+  static constexpr int SFA_COLS = 4 * KPS;
+  static constexpr int SF_STAGE_COLS = SFA_COLS + KPS * SFBC * (DUAL ? 2 : 1);
   static constexpr int TMEM_COLS = 512;
   static constexpr int THREADS = 320;
   static constexpr bool PAIR = true;
@@ -594,6 +600,7 @@ struct Gemm2Cfg {
   static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(256, BN);
   static constexpr uint32_t TX_AB = 2u * (A_BYTES + B_BYTES * (DUAL ? 2 : 1));   // both CTAs' operand bytes
   static_assert(BN % 64 == 0 && BN <= 256 && (BN % 128 == 0 || BN == 64), "pair tile N");
+  static_assert(KA == 1 || SFTMA_, "wide stages load scales by tensor map");
   static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
@@ -661,14 +668,13 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
         const int local = t - G.tile_begin;
         const int mt = local % G.tiles_m, nt = local / G.tiles_m;
-        const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+        const int nk64 = G.K / 64, nks = (nk64 + C::KPS - 1) / C::KPS;
         const int rt_a = mt * 2 + (int)cta;
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const uint32_t fb_leader = mapa(bar_full + 8 * s, 0);
-          const int nch = min(4, nk64 - 4 * ks);
           if (C::DBG & 4) {
             mbar_arrive(bar_sff + 8 * s);
             mbar_arrive(bar_opf + 8 * s);
@@ -677,16 +683,21 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           // this CTA's scales first, on their own local barrier, so the scale
           // warps stage them into tensor memory while the operands are in flight
           const uint32_t lb = bar_sff + 8 * s, ob = bar_opf + 8 * s;
-          mbar_arrive_expect_tx(lb, (C::DBG & 16) ? 0 : 2048 + C::SFB_BYTES * (C::DUAL ? 2 : 1));
+          mbar_arrive_expect_tx(lb, (C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1));
           mbar_arrive_expect_tx(ob, C::TX_AB / 2);
-          tma_load_2d(st, &G.ta, ob, ks * KSTEP_BYTES, rt_a * BM, pol_a);
-          tma_load_2d(st + C::OFF_B, &G.tb, ob, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB, pol_b);
-          if (C::DUAL) tma_load_2d(st + C::OFF_B2, &G.tb2, ob, ks * KSTEP_BYTES, nt * C::BN + (int)cta * C::HB, pol_b);
+#pragma unroll
+          for (int a = 0; a < C::KA; ++a) {
+            const int x = (ks * C::KA + a) * KSTEP_BYTES;
+            tma_load_2d(st + a * C::A_ATOM, &G.ta, ob, x, rt_a * BM, pol_a);
+            tma_load_2d(st + C::OFF_B + a * C::B_ATOM, &G.tb, ob, x, nt * C::BN + (int)cta * C::HB, pol_b);
+            if (C::DUAL)
+              tma_load_2d(st + C::OFF_B2 + a * C::B_ATOM, &G.tb2, ob, x, nt * C::BN + (int)cta * C::HB, pol_b);
+          }
           if (!(C::DBG & 16)) {
             if (C::SFTMA) {
-              tma_load_3d(st + C::OFF_SFA, &G.tsa, lb, 0, 4 * ks, rt_a, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, lb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, lb, 0, 4 * ks, (nt * C::BN) / 128, pol_b);
+              tma_load_3d(st + C::OFF_SFA, &G.tsa, lb, 0, C::KPS * ks, rt_a, pol_a);
+              tma_load_3d(st + C::OFF_SFB, &G.tsb, lb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
+              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, lb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
             } else {
               load_sf_bulk<C>(st, G, rt_a, (nt * C::BN) / 128, nk64, ks, lb);
             }
@@ -700,7 +711,7 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
       uint32_t it = 0, tile_it = 0;
       for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-        const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+        const int nk64 = G.K / 64, nks = (nk64 + C::KPS - 1) / C::KPS;
         const uint32_t sfb_off = (uint32_t)((((t - G.tile_begin) / G.tiles_m) * C::BN) % 128) / 32;
         if (!mbar_wait_cluster(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
         tc::fence_after_sync();
@@ -711,18 +722,20 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           if (!mbar_wait_cluster(bar_sfr + 8 * s, ph, P.err, kDevErrTimeoutFull)) goto done;
           tc::fence_after_sync();
           const uint32_t st = sbase + s * C::STAGE_BYTES;
-          const int nch = min(4, nk64 - 4 * ks);
+          const int nch = min(C::KPS, nk64 - C::KPS * ks);
           const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
-          const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFBC;
-          const uint64_t da = tc::desc_sw128(st), db = tc::desc_sw128(st + C::OFF_B);
-          const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2);
+          const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFBC;
           for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-            tc::mma_mxf4nvf4_pair(tmem, da + 2 * kk, db + 2 * kk, C::IDESC, sfa_t + 4 * kk,
-                                  sfb_t + kk * C::SFBC + sfb_off, accum);
-            if (C::DUAL)
-              tc::mma_mxf4nvf4_pair(tmem + C::BN, da + 2 * kk, db2 + 2 * kk, C::IDESC, sfa_t + 4 * kk,
+            const int at = kk >> 2, sl = kk & 3;   // K atom of the stage, 64-element slice in it
+            const uint64_t da = tc::desc_sw128(st + at * C::A_ATOM) + 2 * sl;
+            const uint64_t db = tc::desc_sw128(st + C::OFF_B + at * C::B_ATOM) + 2 * sl;
+            tc::mma_mxf4nvf4_pair(tmem, da, db, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFBC + sfb_off, accum);
+            if (C::DUAL) {
+              const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2 + at * C::B_ATOM) + 2 * sl;
+              tc::mma_mxf4nvf4_pair(tmem + C::BN, da, db2, C::IDESC, sfa_t + 4 * kk,
                                     sfb2_t + kk * C::SFBC + sfb_off, accum);
+            }
           }
           tc::commit_pair_both(bar_empty + 8 * s, 3);
         }
@@ -737,14 +750,14 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
     uint32_t it = 0;
     for (int t = pair; t < P.total_tiles; t += npairs) {
       const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-      const int nk64 = G.K / 64, nks = (nk64 + 3) / 4;
+      const int nk64 = G.K / 64, nks = (nk64 + C::KPS - 1) / C::KPS;
       for (int ks = 0; ks < nks; ++ks, ++it) {
         const int s = it % C::STAGES;
         if (!mbar_wait(bar_sff + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
         const uint8_t* st = smem_raw + s * C::STAGE_BYTES;
-        const int nch = min(4, nk64 - 4 * ks);
+        const int nch = min(C::KPS, nk64 - C::KPS * ks);
         const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
-        const uint32_t sfa_t = sf, sfb_t = sf + 16, sfb2_t = sf + 16 + 4 * C::SFBC;
+        const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFBC;
         for (int kk = 0; kk < nch && !(C::DBG & 1); ++kk) {
           const uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
           tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
@@ -754,8 +767,8 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_const
           for (int op = 0; op < (C::DUAL ? 2 : 1); ++op) {
 #pragma unroll
             for (int nb = 0; nb < C::NB; ++nb) {
-              const uint4 w = *reinterpret_cast<const uint4*>(st + (op ? C::OFF_SFB2 : C::OFF_SFB) + nb * 2048 +
-                                                              kk * 512 + lane * 16);
+              const uint4 w = *reinterpret_cast<const uint4*>(st + (op ? C::OFF_SFB2 : C::OFF_SFB) +
+                                                              nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
               tc::st_32x32b_x4((op ? sfb2_t : sfb_t) + kk * C::SFBC + 4 * nb, w.x, w.y, w.z, w.w);
             }
           }
