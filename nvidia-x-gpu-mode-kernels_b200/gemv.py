@@ -81,3 +81,43 @@ def custom_kernel(a, b=None, scale_a=None, scale_b=None, c=None):
     else:
         gemv_raw(a, b, scale_a, scale_b, c, M, K, L)
     return c
+
+
+def nvfp4_gemv_forward(a, b, sa, sb, c, M: int, K: int, L: int) -> None:
+    """The reference's own entry point, same name, arguments and in-place
+    semantics (blackwell_nvfp4_gemv.cu:500-524): computes the first M rows, K
+    elements and L batches of the given tensors into ``c`` and returns None.
+
+    The reference trusts M, K and L; here they must fit inside the tensors
+    (ValueError otherwise: larger values would read past them), K must be a
+    multiple of 16, and the tensors must be CUDA tensors of the dtypes
+    ``custom_kernel`` accepts.  Strides come from the tensors, as in the
+    reference.
+    """
+    M, K, L = int(M), int(K), int(L)
+    for name, t in (("a", a), ("b", b), ("sa", sa), ("sb", sb), ("c", c)):
+        if not isinstance(t, torch.Tensor) or t.dim() != 3:
+            raise TypeError(f"{name} must be a 3-D torch.Tensor")
+    if M < 1 or L < 1 or K < 16 or K % 16:
+        raise ValueError(f"need M >= 1, L >= 1 and K a positive multiple of 16 (got M={M}, K={K}, L={L})")
+    if M > a.shape[0] or K // 2 > a.shape[1] or L > a.shape[2]:
+        raise ValueError(f"M={M}, K={K}, L={L} exceed a's shape {tuple(a.shape)}")
+    if K // 2 > b.shape[1] or L > b.shape[2]:
+        raise ValueError(f"K={K}, L={L} exceed b's shape {tuple(b.shape)}")
+    if M > sa.shape[0] or K // 16 > sa.shape[1] or L > sa.shape[2]:
+        raise ValueError(f"M={M}, K={K}, L={L} exceed sa's shape {tuple(sa.shape)}")
+    if K // 16 > sb.shape[1] or L > sb.shape[2]:
+        raise ValueError(f"K={K}, L={L} exceed sb's shape {tuple(sb.shape)}")
+    if M > c.shape[0] or L > c.shape[2]:
+        raise ValueError(f"M={M}, L={L} exceed c's shape {tuple(c.shape)}")
+    if c.dtype != torch.float16:
+        raise TypeError("c must be float16")
+    _check3("a", a, _FP4_DTYPES)
+    _check3("b", b, _FP4_DTYPES)
+    _check3("sa", sa, _FP8_DTYPES)
+    _check3("sb", sb, _FP8_DTYPES)
+    dev = c.device
+    if not (a.device == b.device == sa.device == sb.device == dev):
+        raise ValueError("all tensors must be on one device")
+    with torch.cuda.device(dev):
+        gemv_raw(a, b, sa, sb, c, M, K, L)

@@ -90,3 +90,22 @@ def test_allgather_rejects_bad_world_without_gpu(pkg):
     a = list(args(2, 0))
     a[13] = ctypes.cast(nulls, ctypes.c_void_p)
     assert l.nvfp4_gemv_allgather(*a) == 1 and b"null peer" in l.nvfp4_last_error()
+
+
+def test_gemv_forward_checks_sizes_against_tensors(pkg):
+    """nvfp4_gemv_forward (the reference's binding signature) refuses M, K, L
+    that do not fit the tensors before touching any device."""
+    import torch
+    a = torch.zeros((64, 256, 1), dtype=torch.uint8)
+    b = torch.zeros((1, 256, 1), dtype=torch.uint8)
+    sa = torch.zeros((64, 32, 1), dtype=torch.uint8)
+    sb = torch.zeros((1, 32, 1), dtype=torch.uint8)
+    c = torch.zeros((64, 1, 1), dtype=torch.float16)
+    with pytest.raises(ValueError, match="exceed a"):
+        pkg.nvfp4_gemv_forward(a, b, sa, sb, c, 65, 512, 1)
+    with pytest.raises(ValueError, match="exceed a"):
+        pkg.nvfp4_gemv_forward(a, b, sa, sb, c, 64, 1024, 1)
+    with pytest.raises(ValueError, match="multiple of 16"):
+        pkg.nvfp4_gemv_forward(a, b, sa, sb, c, 64, 40, 1)
+    with pytest.raises(ValueError, match="CUDA"):
+        pkg.nvfp4_gemv_forward(a, b, sa, sb, c, 64, 512, 1)

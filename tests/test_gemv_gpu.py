@@ -157,3 +157,24 @@ def test_gemv_on_side_stream(pkg, oracle, cuda):
         pkg.custom_kernel(*x.as_tuple())
     s.synchronize()
     _check(oracle, x.c.cpu().numpy(), *_to_cpu(x), 300, 2048, 1)
+
+
+def test_gemv_forward_matches_custom_kernel(pkg, oracle, cuda):
+    """The reference's binding signature: the full problem equals custom_kernel
+    bit for bit; a sub-problem (first M rows, first L batches) computes exactly
+    those outputs and leaves the rest of c untouched."""
+    M, K, L = 256, 1024, 2
+    x = pkg.inputs.gemv_inputs(M, K, L, seed=7, device=cuda)
+    pkg.custom_kernel(*x.as_tuple())
+    torch.cuda.synchronize()
+    want = x.c.clone()
+    c = torch.full_like(x.c, float("nan"))
+    assert pkg.nvfp4_gemv_forward(x.a, x.b, x.sfa, x.sfb, c, M, K, L) is None
+    torch.cuda.synchronize()
+    assert torch.equal(c, want)
+    c.fill_(float("nan"))
+    pkg.nvfp4_gemv_forward(x.a, x.b, x.sfa, x.sfb, c, 200, K, 1)
+    torch.cuda.synchronize()
+    assert torch.equal(c[:200, :, :1], want[:200, :, :1])
+    assert torch.isnan(c[200:]).all() and torch.isnan(c[:, :, 1:]).all()
+    assert pkg._lib.device_errors() == 0
