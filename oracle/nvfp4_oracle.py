@@ -153,7 +153,8 @@ def gemv(a, b, sfa, sfb, M: int, K: int, L: int, acc=np.float32) -> np.ndarray:
         A = _dequant_rows(a[:M, : K // 2, l], sfa[:M, : K // 16, l]).astype(acc)
         bv = _dequant_rows(b[:1, : K // 2, l], sfb[:1, : K // 16, l])[0].astype(acc)
         r = A @ bv
-        out[:, 0, l] = r.astype(np.float16) if acc == np.float32 else r
+        with np.errstate(over="ignore"):   # beyond fp16 range the output is inf, as on the GPU
+            out[:, 0, l] = r.astype(np.float16) if acc == np.float32 else r
     return out
 
 
