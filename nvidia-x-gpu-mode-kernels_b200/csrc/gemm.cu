@@ -1039,10 +1039,8 @@ int skinny_run(const void* x, const void* w, const void* sfx, const void* sfw, v
   return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
-template <class C>
-int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
-  constexpr int MAXG = 24;
-  if (!groups || num_groups < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_grouped_gemm: no groups");
+template <class C, int MAXG>
+int grouped_launches(const nvfp4_group* groups, int num_groups, void* stream) {
   uint32_t* err = device_error_word();
   if (!err) return fail(NVFP4_ERR_CUDA, "nvfp4_grouped_gemm: cannot resolve the device error word");
   static GemmParams<MAXG> P;          // large; built under a lock, copied into the launch
@@ -1086,6 +1084,16 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
     if (rc) return rc;
   }
   return NVFP4_OK;
+}
+
+// The kernel parameters carry every group's tensor maps (about 1 KB a group):
+// up to 8 groups launch with an 8-group parameter block instead of paying for
+// 24 groups' worth on every launch.
+template <class C>
+int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
+  if (!groups || num_groups < 1) return fail(NVFP4_ERR_INVALID, "nvfp4_grouped_gemm: no groups");
+  if (num_groups <= 8) return grouped_launches<C, 8>(groups, num_groups, stream);
+  return grouped_launches<C, 24>(groups, num_groups, stream);
 }
 }  // namespace nvfp4
 
