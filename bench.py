@@ -414,7 +414,7 @@ def our_arm(args, world, rank, local):
         barrier(world)
         t_wall = time.perf_counter() - t_wall0
     step_ms = [sum(s) for s in segs]
-    mean_step, = max_over_ranks(world, [statistics.mean(step_ms)])
+    mean_step, median_step = max_over_ranks(world, [statistics.mean(step_ms), statistics.median(step_ms)])
     if world > 1:
         # the same rows through the plain kernel + an NCCL all-gather, for comparison
         nsegs = time_steps(step_nccl, args.steps, args.warmup, flush, align=align)
@@ -459,6 +459,7 @@ def our_arm(args, world, rank, local):
         "metric": "NVFP4 GEMV HBM GB/s (M=K=16384, L=1)",
         "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(mean_step, 5), "us_per_step": round(mean_step * 1e3, 3),
+        "us_per_step_median": round(median_step * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e2m1/e4m3 in, f32 acc, f16 out",
         "data": "synthetic (seed 0; codes uniform 0..255, scales 2^u, u in [-3,3])",
         "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1" +
