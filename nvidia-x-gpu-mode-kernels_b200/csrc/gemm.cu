@@ -2,28 +2,34 @@
 //
 //   grouped:  C_g[M_g, N_g] = A_g[M_g, K_g] . B_g[N_g, K_g]^T          (fp16 out)
 //   dual:     C[M, N] = silu(A . B1^T) * (A . B2^T)                    (fp16 out)
+//   skinny:   out[T, N] = X[T, K] . W[N, K]^T, T <= 64 (weights as the MMA's
+//             128-row operand, the epilogue writes C^T)
 //
 // Operands are e2m1 codes packed two per byte, K-major (rows of K/2 bytes),
 // with one e4m3 scale per 16 K-elements stored in the 128x4 blocked layout
 // (128-row x 4-scale tiles of 512 bytes, row-tile major; inside a tile the
-// scale (r, c) sits at byte (r%32)*16 + (r/32)*4 + c).  That layout is what a
-// tcgen05.cp 32x128b.warpx4 copy turns into the tensor-memory arrangement the
-// block-scaled MMA reads, so scales go global -> shared -> tensor memory with
-// plain copies.  The MMA reads scales as unsigned e4m3 (sign bit must be 0).
+// scale (r, c) sits at byte (r%32)*16 + (r/32)*4 + c).  That layout is the
+// image a 32x128b.warpx4 copy turns into the tensor-memory arrangement the
+// block-scaled MMA reads.  The MMA reads scales as unsigned e4m3 (sign bit 0).
 //
-// One persistent CTA per SM walks output tiles of 128 x BN (tile t, t+grid,
-// ...).  Tiles of a group are ordered M-tile fastest, so CTAs running at the
-// same time share B tiles through L2.  Warp roles:
-//   warp 0  TMA producer: per 256-element K step, one 128x128-byte box of A and
-//           one BNx128-byte box of B (and B2) with 128-byte swizzle, plus 1-D
-//           bulk copies of the 2 KB scale blocks, into a STAGES-deep ring;
-//   warp 1  allocates tensor memory; one thread copies the stage's scales into
-//           tensor memory and issues 4 MMAs of K=64 (kind::mxf4nvf4,
-//           scale_vec::4X) per B operand, then commits the stage back to the
-//           producer and, after the last K step, the accumulator to the
-//           epilogue;
-//   warps 2-5  epilogue: tcgen05.ld of the fp32 accumulator rows (one row per
-//           thread), SiLU-gate or plain conversion to fp16, 16-byte stores.
+// gemm_kernel (gemm_kernel.cuh): one persistent CTA per SM walks output tiles
+// of 128 x BN (tile t, t+grid, ...); tiles of a group are ordered M-tile
+// fastest, so CTAs running at the same time share B tiles through L2.  A stage
+// holds KA 128-byte K atoms (256 elements each).  Warp roles:
+//   warp 0     TMA producer: per stage, tensor-map boxes of the stage's scale
+//              blocks (on their own barrier, issued first) and one 128-byte
+//              swizzled box per K atom of A and of B (and B2);
+//   warp 1     allocates tensor memory; one thread issues 4*KA MMAs of K=64
+//              (kind::mxf4nvf4, scale_vec::4X) per B operand, commits the
+//              stage back to the producer and, after the last K step, the
+//              accumulator to the epilogue;
+//   warps 2-5  epilogue: tcgen05.ld of the fp32 accumulator (one row per
+//              thread), SiLU gate or plain conversion to fp16, 16-byte stores;
+//              the grouped GEMM drains the whole row to registers and releases
+//              the accumulator before storing;
+//   warps 6-9  scale warps: copy each stage's scale blocks from shared memory
+//              into tensor memory with tcgen05.st, each its lane quarter.
+// gemm2_kernel (gemm_pair.cuh) is the CTA-pair variant, kept for the record.
 // Every mbarrier wait is bounded (2 s) and reports into the device error word.
 #include <cuda_fp16.h>
 #include <cstring>
@@ -33,818 +39,11 @@
 #include "common.h"
 #include "tmap.h"
 
+#include "gemm_cfg.cuh"
+#include "gemm_kernel.cuh"
+#include "gemm_pair.cuh"
+
 namespace nvfp4 {
-namespace {
-
-constexpr int BM = 128;          // rows per tile (one MMA of M=128)
-constexpr int KSTEP = 256;       // K elements per stage = 128 bytes per row
-constexpr int KSTEP_BYTES = 128;
-
-struct GemmGroup {
-  CUtensorMap ta, tb, tb2;       // A [M, K/2], B [N, K/2] (B2 for the dual GEMM)
-  CUtensorMap tc;                // C [M, N] fp16, 64-column boxes, 128-byte swizzle
-  CUtensorMap tsa, tsb, tsb2;    // blocked scales as [row tiles][K/64][128 x u32]
-  const uint8_t* sfa;            // blocked scales of A, B, B2
-  const uint8_t* sfb;
-  const uint8_t* sfb2;
-  __half* c;
-  int64_t ldc;                   // elements
-  int M, N, K;
-  int tiles_m, tiles_n, tile_begin;
-  int vec_ok;                    // c 16-byte aligned and ldc % 8 == 0: 16-byte stores
-  int tma_store;                 // tc is valid: the epilogue stores through shared memory + TMA
-};
-
-template <int MAXG>
-struct GemmParams {
-  GemmGroup g[MAXG];
-  int ngroups;
-  int total_tiles;
-  uint32_t* err;
-};
-
-// DBG is a tuning knob (0 in every product instantiation): bit 0 skips the
-// scale copies, bit 1 the MMAs, bit 2 the loads, bit 3 the epilogue's
-// tensor-memory loads and stores, to time each link alone.
-// SFST selects how block scales reach tensor memory: 0 = tcgen05.cp issued by
-// the MMA thread, 1 = four scale warps that tcgen05.st them (off the MMA queue).
-// EPI 1 stages the fp16 tile in shared memory and writes it with TMA stores
-// (needs BM*BN*2 bytes of shared memory); EPI 0 stores rows from registers.
-// POL picks the L2 policy of B loads: 0 evict-first, 1 normal.
-// SEPSF 1: the stage's scale boxes complete on their own barrier, issued
-// before the operand boxes, so the scale warps stage them while the operand
-// bytes are still in flight (needs SFST and SFTMA).
-// TRANS 1 (skinny GEMM): A holds weight rows, B the token rows, and the
-// epilogue writes C^T, i.e. out[token][weight row]; one N tile only.
-template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFST_ = 1, int EPI_ = 1, int POL_ = 0, int SFTMA_ = 1,
-          int SEPSF_ = 1, int TRANS_ = 0, int KA_ = 1>
-struct GemmCfg {
-  static constexpr int TRANS = TRANS_;
-  // KA 128-byte K atoms (256 elements each) per stage: one TMA box per atom and
-  // operand, 4 * KA MMAs per stage, scale boxes of 4 * KA K-blocks
-  static constexpr int KA = KA_;
-  static constexpr int KPS = 4 * KA_;    // 64-element K blocks per stage
-  static constexpr int SFTMA = SFTMA_;   // scales by tensor-map TMA (1) or 1-D bulk copies (0)
-  static constexpr int SEPSF = (SEPSF_ && SFST_ && SFTMA_) ? 1 : 0;
-  static constexpr int DBG = DBG_;
-  static constexpr int EPI = EPI_;
-  static constexpr int POL = POL_;
-  static constexpr int SFST = SFST_;
-  static constexpr int BN = BN_;
-  static constexpr bool DUAL = DUAL_;
-  static constexpr int STAGES = STAGES_;
-  static constexpr int NB = (BN + 127) / 128;              // 128-row scale blocks per B tile
-  static_assert(BN % 128 == 0 || (BN < 128 && 128 % BN == 0 && (BN % 32 == 0 || (TRANS_ && BN == 16))),
-                "B tiles must not straddle scale blocks");
-  static constexpr int A_ATOM = BM * KSTEP_BYTES;          // 16 KB per K atom
-  static constexpr int B_ATOM = BN * KSTEP_BYTES;
-  static constexpr int A_BYTES = KA * A_ATOM;
-  static constexpr int B_BYTES = KA * B_ATOM;
-  static constexpr int SFA_BYTES = KPS * 512;              // KPS K-blocks of 64
-  static constexpr int SFB_ROWTILE = KPS * 512;            // per 128-row block of B
-  static constexpr int SFB_BYTES = NB * SFB_ROWTILE;
-  static constexpr int OFF_B = A_BYTES;
-  static constexpr int OFF_B2 = OFF_B + B_BYTES;
-  static constexpr int OFF_SFA = OFF_B2 + (DUAL ? B_BYTES : 0);
-  static constexpr int OFF_SFB = OFF_SFA + SFA_BYTES;
-  static constexpr int OFF_SFB2 = OFF_SFB + SFB_BYTES;
-  static constexpr int STAGE_BYTES = ((OFF_SFB2 + (DUAL ? SFB_BYTES : 0)) + 1023) / 1024 * 1024;
-  static constexpr int OFF_C = STAGES * STAGE_BYTES;      // fp16 output tile, BN/64 swizzled boxes
-  static constexpr int C_BYTES = EPI ? BM * BN * 2 : 0;
-  static constexpr int OFF_BAR = OFF_C + C_BYTES;
-  static constexpr int SMEM = OFF_BAR + (4 * STAGES + 4) * 8 + 16;   // base is 1024-aligned
-  // tensor memory columns
-  static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
-  static constexpr int SF_BASE = ACC_COLS;
-  static constexpr int SFB_COLS_PER_KB = NB * 4;
-  static constexpr int SFA_COLS = 4 * KPS;
-  static constexpr int SF_STAGE_COLS = SFA_COLS + KPS * SFB_COLS_PER_KB * (DUAL ? 2 : 1);
-  static constexpr int TMEM_COLS = 512;
-  static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
-  static_assert(KA == 1 || SFTMA_, "wide stages load scales by tensor map");
-  static_assert(SMEM <= 232448, "shared memory budget");
-  static constexpr int THREADS = SFST ? 320 : 192;   // + 4 scale warps (warps 6-9)
-  static constexpr bool PAIR = false;
-  static constexpr int TILE_M = BM;
-  static constexpr int B_BOX = BN;
-  static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(BM, BN);
-};
-
-__device__ __forceinline__ int find_group(const GemmGroup* g, int ng, int t) {
-  int i = 0;
-  while (i + 1 < ng && g[i + 1].tile_begin <= t) ++i;
-  return i;
-}
-
-// Scale blocks of one 256-element K step with 1-D bulk copies: the A row
-// tile and the B row tiles [rt_b, rt_b + NB).  The caller registered the
-// full-box byte count (as for tensor-map loads); bytes that are not copied
-// (blocks past the end of a matrix or of K) are completed here directly.
-template <class C>
-__device__ __forceinline__ void load_sf_bulk(uint32_t st, const GemmGroup& G, int rt_a, int rt_b, int nk64, int ks,
-                                             uint32_t bar) {
-  const int nch = min(4, nk64 - 4 * ks);
-  const int nrt_a = (G.M + 127) / 128, nrt_b = (G.N + 127) / 128;
-  uint32_t missing = 0;
-  if (rt_a < nrt_a) bulk_g2s(st + C::OFF_SFA, G.sfa + ((size_t)rt_a * nk64 + 4 * ks) * 512, nch * 512, bar);
-  missing += (rt_a < nrt_a) ? (4 - nch) * 512 : 2048;
-  for (int nb = 0; nb < C::NB; ++nb) {
-    const int rt = rt_b + nb;
-    const int ops = C::DUAL ? 2 : 1;
-    if (rt >= nrt_b) { missing += 2048 * ops; continue; }
-    bulk_g2s(st + C::OFF_SFB + nb * 2048, G.sfb + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, bar);
-    if (C::DUAL) bulk_g2s(st + C::OFF_SFB2 + nb * 2048, G.sfb2 + ((size_t)rt * nk64 + 4 * ks) * 512, nch * 512, bar);
-    missing += (4 - nch) * 512 * ops;
-  }
-  if (missing) {   // complete the uncopied bytes ourselves
-    asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(missing) : "memory");
-  }
-}
-
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  return __fdividef(g, 1.0f + __expf(-g)) * u;
-}
-
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// The first n (<= 8) fp16 values of a packed 16-byte piece, one element at a
-// time (unaligned or ragged output rows).  Out of line so the epilogue's
-// unrolled row loop does not hold a store path per element in registers.
-__device__ __noinline__ void store_piece(__half* dst, uint4 piece, int n) {
-  const uint32_t w[4] = {piece.x, piece.y, piece.z, piece.w};
-  for (int j = 0; j < n; ++j) dst[j] = __ushort_as_half((unsigned short)(w[j / 2] >> (16 * (j & 1))));
-}
-
-template <class C, int MAXG>
-__global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams<MAXG> P) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t sbase = raw;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  if (raw & 1023u) {  // the swizzled tiles need a 1024-aligned base; the launch guarantees it
-    if (threadIdx.x == 0) atomicOr(P.err, kDevErrTimeoutMma);
-    return;
-  }
-  const uint32_t bar_full = sbase + C::OFF_BAR;
-  const uint32_t bar_empty = bar_full + 8 * C::STAGES;
-  const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;      // scales in tensor memory (SFST)
-  const uint32_t bar_sff = bar_sfr + 8 * C::STAGES;        // scale boxes landed (SEPSF)
-  const uint32_t bar_accf = bar_sff + 8 * C::STAGES;
-  const uint32_t bar_acce = bar_accf + 8;
-  const uint32_t bar_done = bar_acce + 8;
-  const uint32_t tmem_slot = bar_done + 8;
-  volatile uint32_t* tmem_slot_ptr =
-      reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, 1);
-      mbar_init(bar_sfr + 8 * s, 4);
-      mbar_init(bar_sff + 8 * s, 1);
-    }
-    mbar_init(bar_accf, 1);
-    mbar_init(bar_acce, 4);
-    mbar_init(bar_done, 1);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tc::tmem_relinquish();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot_ptr;
-
-  if (warp == 0) {
-    // ---------------------------- producer ----------------------------
-    if (lane == 0) {
-      for (int i = 0; i < P.ngroups; ++i) {
-        prefetch_tmap(&P.g[i].ta);
-        prefetch_tmap(&P.g[i].tb);
-        if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
-        if (C::SFTMA) {
-          prefetch_tmap(&P.g[i].tsa);
-          prefetch_tmap(&P.g[i].tsb);
-          if (C::DUAL) prefetch_tmap(&P.g[i].tsb2);
-        }
-      }
-      const uint64_t pol_a = policy_evict_last();   // A tiles are re-read by every N tile
-      const uint64_t pol_b = C::POL ? policy_evict_normal() : policy_evict_first();
-      uint32_t it = 0;
-      for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
-        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-        const int local = t - G.tile_begin;
-        const int mt = local % G.tiles_m, nt = local / G.tiles_m;
-        const int nk64 = G.K / 64;
-        const int nks = (nk64 + C::KPS - 1) / C::KPS;
-        for (int ks = 0; ks < nks; ++ks, ++it) {
-          const int s = it % C::STAGES;
-          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
-          const uint32_t st = sbase + s * C::STAGE_BYTES;
-          const uint32_t fb = bar_full + 8 * s;
-          // scale boxes always count in full (blocks past the end read as zeros)
-          const uint32_t sf_bytes = (C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1);
-          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) + (C::SEPSF ? 0 : sf_bytes);
-          if (C::DBG & 4) {
-            mbar_arrive(fb);
-            if (C::SEPSF) mbar_arrive(bar_sff + 8 * s);
-            continue;
-          }
-          if (C::SEPSF) {   // scales first, on their own barrier
-            const uint32_t sb = bar_sff + 8 * s;
-            mbar_arrive_expect_tx(sb, sf_bytes);
-            if (!(C::DBG & 16)) {
-              tma_load_3d(st + C::OFF_SFA, &G.tsa, sb, 0, C::KPS * ks, mt, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, sb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, sb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-            }
-          }
-          mbar_arrive_expect_tx(fb, bytes);
-#pragma unroll
-          for (int a = 0; a < C::KA; ++a) {   // atoms past K read as zeros (and count in full)
-            const int x = (ks * C::KA + a) * KSTEP_BYTES;
-            tma_load_2d(st + a * C::A_ATOM, &G.ta, fb, x, mt * BM, pol_a);
-            tma_load_2d(st + C::OFF_B + a * C::B_ATOM, &G.tb, fb, x, nt * C::BN, pol_b);
-            if (C::DUAL) tma_load_2d(st + C::OFF_B2 + a * C::B_ATOM, &G.tb2, fb, x, nt * C::BN, pol_b);
-          }
-          if (!(C::DBG & 16) && !C::SEPSF) {
-            if (C::SFTMA) {
-              tma_load_3d(st + C::OFF_SFA, &G.tsa, fb, 0, C::KPS * ks, mt, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, fb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, fb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-            } else {
-              load_sf_bulk<C>(st, G, mt, (nt * C::BN) / 128, nk64, ks, fb);
-            }
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------ MMA -------------------------------
-    if (lane == 0) {
-      uint32_t it = 0, tile_it = 0;
-      for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
-        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-        const int nk64 = G.K / 64;
-        const int nks = (nk64 + C::KPS - 1) / C::KPS;
-        // a B tile narrower than 128 rows starts inside its scale block: its
-        // scales begin (tile row offset / 32) columns into the block's 4
-        const uint32_t sfb_off = (uint32_t)((((t - G.tile_begin) / G.tiles_m) * C::BN) % 128) / 32;
-        if (!mbar_wait(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
-        tc::fence_after_sync();
-        for (int ks = 0; ks < nks; ++ks, ++it) {
-          const int s = it % C::STAGES;
-          if (!mbar_wait((C::SFST ? bar_sfr : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull))
-            goto done;
-          if (C::SEPSF && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
-          tc::fence_after_sync();
-          const uint32_t st = sbase + s * C::STAGE_BYTES;
-          const int nch = min(C::KPS, nk64 - C::KPS * ks);
-          const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
-          const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFB_COLS_PER_KB;
-          for (int kk = 0; kk < nch && !(C::DBG & 1) && !C::SFST; ++kk) {
-            tc::cp_sf_32x128b_x4(sfa_t + 4 * kk, tc::desc_sf_block(st + C::OFF_SFA + kk * 512));
-            for (int nb = 0; nb < C::NB; ++nb) {
-              tc::cp_sf_32x128b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
-                                   tc::desc_sf_block(st + C::OFF_SFB + nb * C::SFB_ROWTILE + kk * 512));
-              if (C::DUAL)
-                tc::cp_sf_32x128b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
-                                     tc::desc_sf_block(st + C::OFF_SFB2 + nb * C::SFB_ROWTILE + kk * 512));
-            }
-          }
-          for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
-            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-            // atom kk / 4 of the stage; its (kk % 4)-th 64-element slice starts
-            // 32 bytes further (encoded >> 4)
-            const int at = kk >> 2, sl = kk & 3;
-            const uint64_t da = tc::desc_sw128(st + at * C::A_ATOM) + 2 * sl;
-            const uint64_t db = tc::desc_sw128(st + C::OFF_B + at * C::B_ATOM) + 2 * sl;
-            tc::mma_mxf4nvf4(tmem, da, db, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
-            if (C::DUAL) {
-              const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2 + at * C::B_ATOM) + 2 * sl;
-              tc::mma_mxf4nvf4(tmem + C::BN, da, db2, C::IDESC, sfa_t + 4 * kk,
-                               sfb2_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
-            }
-          }
-          tc::commit(bar_empty + 8 * s);
-        }
-        tc::commit(bar_accf);
-      }
-    }
-  } else if (warp >= 6) {
-    // ------------------- scale warps (SFST == 1 only) -------------------
-    // Each warp copies, for its tensor-memory lane quarter, the 16 bytes of
-    // every 512-byte scale block of the stage (row `lane` of the block) into 4
-    // consecutive columns: the same image a 32x128b.warpx4 copy would make.
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    uint32_t it = 0;
-    bool dead = false;
-    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
-      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-      const int nk64 = G.K / 64;
-      const int nks = (nk64 + C::KPS - 1) / C::KPS;
-      for (int ks = 0; ks < nks; ++ks, ++it) {
-        const int s = it % C::STAGES;
-        if (!dead && !mbar_wait((C::SEPSF ? bar_sff : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err,
-                                kDevErrTimeoutFull))
-          dead = true;
-        if (dead) break;
-        const uint8_t* st = smem_raw + (sbase - raw) + s * C::STAGE_BYTES;
-        const int nch = min(C::KPS, nk64 - C::KPS * ks);
-        const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
-        const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFB_COLS_PER_KB;
-        for (int kk = 0; kk < nch && !(C::DBG & 1); ++kk) {
-          uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
-          tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
-#pragma unroll
-          for (int nb = 0; nb < C::NB; ++nb) {
-            v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB + nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
-            tc::st_32x32b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
-            if (C::DUAL) {
-              v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB2 + nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
-              tc::st_32x32b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
-            }
-          }
-        }
-        tc::wait_st();
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_sfr + 8 * s);
-      }
-      if (dead) break;
-    }
-  } else {
-    // ---------------------------- epilogue ----------------------------
-    const int sub = warp & 3;                 // tensor-memory lane quarter of this warp
-    const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
-    uint32_t tile_it = 0;
-    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
-      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-      const int local = t - G.tile_begin;
-      const int mt = local % G.tiles_m, nt = local / G.tiles_m;
-      if (!mbar_wait(bar_accf, tile_it & 1, P.err, kDevErrTimeoutMma)) break;
-      tc::fence_after_sync();
-      const int rloc = sub * 32 + lane;        // row of the tile held by this thread
-      const int row = mt * BM + rloc;
-      if constexpr (C::TRANS) {
-        // C^T: this thread's accumulator row is output column `row`; its BN
-        // columns are tokens.  A warp stores 32 consecutive output columns of
-        // one token per instruction.
-        constexpr int CHUNK = C::BN < 32 ? C::BN : 32;
-#pragma unroll 1
-        for (int cb = 0; cb < C::BN / CHUNK; ++cb) {
-          uint32_t v[32];
-          if constexpr (CHUNK == 32) tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
-          else tc::ld_32x32b_x16(tmem + lane_base + cb * CHUNK, v);
-          tc::wait_ld();
-          if (cb == C::BN / CHUNK - 1) {
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acce);
-          }
-          if (row < G.M) {
-#pragma unroll
-            for (int j = 0; j < CHUNK; ++j) {
-              const int tok = nt * C::BN + cb * CHUNK + j;
-              if (tok < G.N) G.c[(int64_t)tok * G.ldc + row] = __float2half_rn(__uint_as_float(v[j]));
-            }
-          }
-        }
-        continue;
-      }
-      if (!(C::EPI && G.tma_store) && !(C::DBG & 8) && !C::DUAL) {
-        // Drain the whole accumulator row into registers (packed fp16) and
-        // release it before storing anything, so the next tile's MMAs run while
-        // this tile's global stores drain.  Storing chunk by chunk between the
-        // tensor-memory loads held the accumulator ~3 us per tile (the 16-byte
-        // row-strided stores are slow to issue).  The dual GEMM keeps the
-        // chunked order below: with ~1.5 tiles per CTA its last epilogue is on
-        // the critical path, where interleaving loads and stores is shorter
-        // (31.7 vs 33.4 us on the dual workload; 74.1 vs 74.9 grouped).
-        uint32_t h[C::BN / 2];
-#pragma unroll
-        for (int cb = 0; cb < C::BN / 16; ++cb) {   // 16 columns per load keeps the live set small
-          uint32_t v[32];
-          tc::ld_32x32b_x16(tmem + lane_base + cb * 16, v);
-          tc::wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) h[cb * 8 + j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acce);
-        if (row < G.M) {
-          __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
-          const int col0 = nt * C::BN;
-          const bool vec = col0 + C::BN <= G.N && G.vec_ok;
-#pragma unroll
-          for (int q = 0; q < C::BN / 8; ++q) {   // 8 columns per piece; h stays register-indexed
-            if (vec) {
-              reinterpret_cast<uint4*>(crow)[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-            } else if (col0 + 8 * q < G.N) {
-              store_piece(crow + 8 * q, make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]),
-                          min(8, G.N - col0 - 8 * q));
-            }
-          }
-        }
-        continue;
-      }
-      if (C::EPI && G.tma_store) {
-        // previous tile's TMA stores must have finished reading the staging tile
-        if (threadIdx.x == 64) bulk_wait_read_all();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-      }
-      __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
-#pragma unroll 1
-      for (int cb = 0; cb < C::BN / 32 && !(C::DBG & 8); ++cb) {
-        uint32_t v[32];
-        tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
-        uint32_t h[16];
-        if constexpr (C::DUAL) {
-          uint32_t u[32];
-          tc::ld_32x32b_x32(tmem + lane_base + C::BN + cb * 32, u);
-          tc::wait_ld();
-          if (cb == C::BN / 32 - 1) {   // accumulator fully read: let the next tile's MMAs start
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acce);
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            h[j] = pack_h2(silu_mul(__uint_as_float(v[2 * j]), __uint_as_float(u[2 * j])),
-                           silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
-        } else {
-          tc::wait_ld();
-          if (cb == C::BN / 32 - 1) {
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acce);
-          }
-#pragma unroll
-          for (int j = 0; j < 16; ++j) h[j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        }
-        if (C::EPI && G.tma_store) {
-          // box cb/2 holds 64 columns: row rloc at 128 * rloc, 16-byte chunk q at (q ^ (rloc % 8))
-          uint8_t* box = smem_raw + C::OFF_C + (cb >> 1) * (BM * 128) + rloc * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = ((cb & 1) * 4 + q) ^ (rloc & 7);
-            *reinterpret_cast<uint4*>(box + chunk * 16) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-          }
-          continue;
-        }
-        const int col0 = nt * C::BN + cb * 32;
-        if (row < G.M) {
-          if (col0 + 32 <= G.N && G.vec_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + cb * 32);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-          } else {
-            const __half* hs = reinterpret_cast<const __half*>(h);
-            for (int j = 0; j < 32 && col0 + j < G.N; ++j) crow[cb * 32 + j] = hs[j];
-          }
-        }
-      }
-      if (C::DBG & 8) {
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acce);
-      }
-      if (C::EPI && G.tma_store && !(C::DBG & 8)) {
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (threadIdx.x == 64) {
-          for (int b = 0; b < C::BN / 64; ++b)
-            tma_store_2d(&G.tc, sbase + C::OFF_C + b * (BM * 128), nt * C::BN + 64 * b, mt * BM);
-          bulk_commit_group();
-        }
-      }
-    }
-    if (threadIdx.x == 64) bulk_wait_all();
-  }
-done:
-  tc::fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, C::TMEM_COLS);
-  }
-}
-
-// ===========================================================================
-// CTA-pair variant (tcgen05.mma.cta_group::2).  A cluster of two CTAs on two
-// SMs computes a 256 x BN tile: each CTA holds 128 rows of A and BN/2 rows of
-// each B operand in its shared memory and the 128 x BN accumulator of its own
-// rows in its tensor memory; the leader CTA (cluster rank 0) issues every MMA.
-// Against the single-CTA kernel each CTA streams a third fewer bytes per FLOP
-// (B is split across the pair instead of loaded by both), which is what the
-// single-CTA kernel is limited by (shared-memory fill bandwidth per SM).
-//   * each CTA loads its operand halves and its scale blocks with ordinary TMA
-//     into its own shared memory on one local barrier (`sf_full`); the paired
-//     .cta_group::2 load form, which completes on the leader's barrier,
-//     measured slower (loads-only pipeline 65.6 vs 49.3 us on config 4);
-//   * four scale warps per CTA wait for that barrier, write the scales into
-//     this CTA's tensor memory in the
-//     single-CTA arrangement (A: this CTA's 128 rows; B: all BN rows of the
-//     tile, 4 columns per 128-row block, replicated in every lane quarter),
-//     then arrive on the leader's `sf_ready` barrier across the cluster: that
-//     arrival tells the leader this CTA's whole stage is ready;
-//   * the leader commits each stage to both CTAs' `empty` barriers and each
-//     finished accumulator to both CTAs' `accf` with one multicast commit; the
-//     scale warps and the epilogue warps of each CTA meet at a named barrier
-//     and send one arrival per CTA to the leader (`sf_ready`, `acce`).
-// ===========================================================================
-template <int BN_, bool DUAL_, int STAGES_, int DBG_ = 0, int SFTMA_ = 1, int KA_ = 1>
-struct Gemm2Cfg {
-  static constexpr int KA = KA_;                           // 128-byte K atoms per stage (as in GemmCfg)
-  static constexpr int SFTMA = SFTMA_;
-  static constexpr int DBG = DBG_;                         // tuning knob as in GemmCfg (0 in the product)
-  static constexpr int BN = BN_;                           // N per pair MMA (per B operand)
-  static constexpr bool DUAL = DUAL_;
-  static constexpr int STAGES = STAGES_;
-  static constexpr int HB = BN / 2;                        // B rows per CTA
-  static constexpr int KPS = 4 * KA_;                      // 64-element K blocks per stage
-  static constexpr int NB = (BN + 127) / 128;              // 128-row scale blocks of B per tile
-  static constexpr int A_ATOM = BM * KSTEP_BYTES;
-  static constexpr int B_ATOM = HB * KSTEP_BYTES;
-  static constexpr int A_BYTES = KA * A_ATOM;
-  static constexpr int B_BYTES = KA * B_ATOM;
-  static constexpr int OFF_B = A_BYTES;
-  static constexpr int OFF_B2 = OFF_B + B_BYTES;
-  static constexpr int OFF_SFA = OFF_B2 + (DUAL ? B_BYTES : 0);
-  static constexpr int SFA_BYTES = KPS * 512;
-  static constexpr int SFB_ROWTILE = KPS * 512;
-  static constexpr int OFF_SFB = OFF_SFA + SFA_BYTES;
-  static constexpr int SFB_BYTES = NB * SFB_ROWTILE;
-  static constexpr int OFF_SFB2 = OFF_SFB + SFB_BYTES;
-  static constexpr int STAGE_BYTES = ((OFF_SFB2 + (DUAL ? SFB_BYTES : 0)) + 1023) / 1024 * 1024;
-  static constexpr int OFF_BAR = STAGES * STAGE_BYTES;
-  static constexpr int NBARS = 5 * STAGES + 2;
-  static constexpr int SMEM = OFF_BAR + NBARS * 8 + 16;
-  static constexpr int ACC_COLS = DUAL ? 2 * BN : BN;
-  static constexpr int SF_BASE = ACC_COLS;
-  static constexpr int SFBC = NB * 4;                      // B-scale columns per 64-element K block
-  static constexpr int SFA_COLS = 4 * KPS;
-  static constexpr int SF_STAGE_COLS = SFA_COLS + KPS * SFBC * (DUAL ? 2 : 1);
-  static constexpr int TMEM_COLS = 512;
-  static constexpr int THREADS = 320;
-  static constexpr bool PAIR = true;
-  static constexpr int TILE_M = 2 * BM;
-  static constexpr int B_BOX = HB;
-  static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(256, BN);
-  static constexpr uint32_t TX_AB = 2u * (A_BYTES + B_BYTES * (DUAL ? 2 : 1));   // both CTAs' operand bytes
-  static_assert(BN % 64 == 0 && BN <= 256 && (BN % 128 == 0 || BN == 64), "pair tile N");
-  static_assert(KA == 1 || SFTMA_, "wide stages load scales by tensor map");
-  static_assert(SF_BASE + STAGES * SF_STAGE_COLS <= TMEM_COLS, "tensor memory budget");
-  static_assert(SMEM <= 232448, "shared memory budget");
-};
-
-template <class C, int MAXG>
-__global__ void __launch_bounds__(C::THREADS, 1) gemm2_kernel(const __grid_constant__ GemmParams<MAXG> P) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t sbase = smem_u32(smem_raw);
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t cta = cluster_ctarank();
-  const uint32_t pair = cluster_id_x(), npairs = nclusters_x();
-  if (sbase & 1023u) {  // a uniform condition: both CTAs of a pair leave together
-    if (threadIdx.x == 0) atomicOr(P.err, kDevErrTimeoutMma);
-    return;
-  }
-  const uint32_t bar_full = sbase + C::OFF_BAR;            // leader: both CTAs' operand bytes
-  const uint32_t bar_sff = bar_full + 8 * C::STAGES;       // local: this CTA's scale bytes
-  const uint32_t bar_empty = bar_sff + 8 * C::STAGES;      // local: stage consumed by the pair MMAs
-  const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;      // leader: scales of both CTAs in tensor memory
-  const uint32_t bar_accf = bar_sfr + 8 * C::STAGES;       // local: accumulator ready
-  const uint32_t bar_acce = bar_accf + 8;                  // leader: both epilogues drained
-  const uint32_t bar_opf = bar_acce + 8;                   // local: this CTA's operand bytes
-  const uint32_t tmem_slot = bar_opf + 8 * C::STAGES;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(bar_full + 8 * s, 1);
-      mbar_init(bar_sff + 8 * s, 1);
-      mbar_init(bar_empty + 8 * s, 1);
-      mbar_init(bar_sfr + 8 * s, 2);
-      mbar_init(bar_opf + 8 * s, 1);
-    }
-    mbar_init(bar_accf, 1);
-    mbar_init(bar_acce, 2);
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tc::tmem_alloc_pair(tmem_slot, C::TMEM_COLS);
-    tc::tmem_relinquish_pair();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  cluster_sync();   // barriers of both CTAs initialised before any cross-CTA arrival
-  tc::fence_after_sync();
-  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - sbase));
-
-  if (warp == 0) {
-    // --------------------------- producer (both CTAs) ---------------------------
-    if (lane == 0) {
-      for (int i = 0; i < P.ngroups; ++i) {
-        prefetch_tmap(&P.g[i].ta);
-        prefetch_tmap(&P.g[i].tb);
-        if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
-        if (C::SFTMA) {
-          prefetch_tmap(&P.g[i].tsa);
-          prefetch_tmap(&P.g[i].tsb);
-          if (C::DUAL) prefetch_tmap(&P.g[i].tsb2);
-        }
-      }
-      const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_first();
-      uint32_t it = 0;
-      for (int t = pair; t < P.total_tiles; t += npairs) {
-        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-        const int local = t - G.tile_begin;
-        const int mt = local % G.tiles_m, nt = local / G.tiles_m;
-        const int nk64 = G.K / 64, nks = (nk64 + C::KPS - 1) / C::KPS;
-        const int rt_a = mt * 2 + (int)cta;
-        for (int ks = 0; ks < nks; ++ks, ++it) {
-          const int s = it % C::STAGES;
-          if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
-          const uint32_t st = sbase + s * C::STAGE_BYTES;
-          const uint32_t fb_leader = mapa(bar_full + 8 * s, 0);
-          if (C::DBG & 4) {
-            mbar_arrive(bar_sff + 8 * s);
-            mbar_arrive(bar_opf + 8 * s);
-            continue;
-          }
-          // this CTA's scales first, on their own local barrier, so the scale
-          // warps stage them into tensor memory while the operands are in flight
-          const uint32_t lb = bar_sff + 8 * s, ob = bar_opf + 8 * s;
-          mbar_arrive_expect_tx(lb, (C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1));
-          mbar_arrive_expect_tx(ob, C::TX_AB / 2);
-#pragma unroll
-          for (int a = 0; a < C::KA; ++a) {
-            const int x = (ks * C::KA + a) * KSTEP_BYTES;
-            tma_load_2d(st + a * C::A_ATOM, &G.ta, ob, x, rt_a * BM, pol_a);
-            tma_load_2d(st + C::OFF_B + a * C::B_ATOM, &G.tb, ob, x, nt * C::BN + (int)cta * C::HB, pol_b);
-            if (C::DUAL)
-              tma_load_2d(st + C::OFF_B2 + a * C::B_ATOM, &G.tb2, ob, x, nt * C::BN + (int)cta * C::HB, pol_b);
-          }
-          if (!(C::DBG & 16)) {
-            if (C::SFTMA) {
-              tma_load_3d(st + C::OFF_SFA, &G.tsa, lb, 0, C::KPS * ks, rt_a, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, lb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, lb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-            } else {
-              load_sf_bulk<C>(st, G, rt_a, (nt * C::BN) / 128, nk64, ks, lb);
-            }
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ------------------------------ MMA (leader) ------------------------------
-    if (lane == 0 && cta == 0) {
-      uint32_t it = 0, tile_it = 0;
-      for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
-        const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-        const int nk64 = G.K / 64, nks = (nk64 + C::KPS - 1) / C::KPS;
-        const uint32_t sfb_off = (uint32_t)((((t - G.tile_begin) / G.tiles_m) * C::BN) % 128) / 32;
-        if (!mbar_wait_cluster(bar_acce, (tile_it & 1) ^ 1, P.err, kDevErrTimeoutMma)) goto done;
-        tc::fence_after_sync();
-        for (int ks = 0; ks < nks; ++ks, ++it) {
-          const int s = it % C::STAGES;
-          const uint32_t ph = (it / C::STAGES) & 1;
-          // both CTAs' operands landed and their scales are in tensor memory
-          if (!mbar_wait_cluster(bar_sfr + 8 * s, ph, P.err, kDevErrTimeoutFull)) goto done;
-          tc::fence_after_sync();
-          const uint32_t st = sbase + s * C::STAGE_BYTES;
-          const int nch = min(C::KPS, nk64 - C::KPS * ks);
-          const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
-          const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFBC;
-          for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
-            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-            const int at = kk >> 2, sl = kk & 3;   // K atom of the stage, 64-element slice in it
-            const uint64_t da = tc::desc_sw128(st + at * C::A_ATOM) + 2 * sl;
-            const uint64_t db = tc::desc_sw128(st + C::OFF_B + at * C::B_ATOM) + 2 * sl;
-            tc::mma_mxf4nvf4_pair(tmem, da, db, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFBC + sfb_off, accum);
-            if (C::DUAL) {
-              const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2 + at * C::B_ATOM) + 2 * sl;
-              tc::mma_mxf4nvf4_pair(tmem + C::BN, da, db2, C::IDESC, sfa_t + 4 * kk,
-                                    sfb2_t + kk * C::SFBC + sfb_off, accum);
-            }
-          }
-          tc::commit_pair_both(bar_empty + 8 * s, 3);
-        }
-        tc::commit_pair_both(bar_accf, 3);
-      }
-    }
-  } else if (warp >= 6) {
-    // --------------------------- scale warps (both CTAs) ---------------------------
-    const int q = warp & 3;
-    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    const uint32_t sfr_leader = mapa(bar_sfr, 0);
-    uint32_t it = 0;
-    for (int t = pair; t < P.total_tiles; t += npairs) {
-      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-      const int nk64 = G.K / 64, nks = (nk64 + C::KPS - 1) / C::KPS;
-      for (int ks = 0; ks < nks; ++ks, ++it) {
-        const int s = it % C::STAGES;
-        if (!mbar_wait(bar_sff + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
-        const uint8_t* st = smem_raw + s * C::STAGE_BYTES;
-        const int nch = min(C::KPS, nk64 - C::KPS * ks);
-        const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
-        const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFBC;
-        for (int kk = 0; kk < nch && !(C::DBG & 1); ++kk) {
-          const uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
-          tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
-          // B scales: every 128-row block of the tile into 4 columns, in every
-          // lane quarter (the same image as for a single-CTA MMA of N = BN)
-#pragma unroll
-          for (int op = 0; op < (C::DUAL ? 2 : 1); ++op) {
-#pragma unroll
-            for (int nb = 0; nb < C::NB; ++nb) {
-              const uint4 w = *reinterpret_cast<const uint4*>(st + (op ? C::OFF_SFB2 : C::OFF_SFB) +
-                                                              nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
-              tc::st_32x32b_x4((op ? sfb2_t : sfb_t) + kk * C::SFBC + 4 * nb, w.x, w.y, w.z, w.w);
-            }
-          }
-        }
-        tc::wait_st();
-        tc::fence_before_sync();
-        asm volatile("bar.sync 3, 128;" ::: "memory");     // the 4 scale warps of this CTA
-        // once this CTA's operands landed too, its whole stage is ready for the
-        // pair MMA (an expired wait is recorded and the arrival skipped: the
-        // leader's own bounded wait then ends the pipeline)
-        if (threadIdx.x == 192 && mbar_wait(bar_opf + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull))
-          mbar_arrive_cluster(sfr_leader + 8 * s);
-      }
-    }
-  } else {
-    // ----------------------------- epilogue (both CTAs) -----------------------------
-    const int sub = warp & 3;
-    const uint32_t lane_base = (uint32_t)(sub * 32) << 16;
-    const uint32_t acce_leader = mapa(bar_acce, 0);
-    uint32_t tile_it = 0;
-    for (int t = pair; t < P.total_tiles; t += npairs, ++tile_it) {
-      const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
-      const int local = t - G.tile_begin;
-      const int mt = local % G.tiles_m, nt = local / G.tiles_m;
-      if (!mbar_wait(bar_accf, tile_it & 1, P.err, kDevErrTimeoutMma)) break;
-      tc::fence_after_sync();
-      const int row = mt * 256 + (int)cta * BM + sub * 32 + lane;
-      __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
-      // whole accumulator row -> packed fp16 registers, release, then store
-      uint32_t h[C::BN / 2];
-#pragma unroll
-      for (int cb = 0; cb < C::BN / 16; ++cb) {
-        uint32_t v[32];
-        tc::ld_32x32b_x16(tmem + lane_base + cb * 16, v);
-        if constexpr (C::DUAL) {
-          uint32_t u[32];
-          tc::ld_32x32b_x16(tmem + lane_base + C::BN + cb * 16, u);
-          tc::wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            h[cb * 8 + j] = pack_h2(silu_mul(__uint_as_float(v[2 * j]), __uint_as_float(u[2 * j])),
-                                    silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
-        } else {
-          tc::wait_ld();
-#pragma unroll
-          for (int j = 0; j < 8; ++j) h[cb * 8 + j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        }
-      }
-      tc::fence_before_sync();
-      asm volatile("bar.sync 4, 128;" ::: "memory");   // the 4 epilogue warps of this CTA
-      if (threadIdx.x == 64) mbar_arrive_cluster(acce_leader);
-      if (row < G.M) {
-        const int col0 = nt * C::BN;
-        const bool vec = col0 + C::BN <= G.N && G.vec_ok;
-#pragma unroll
-        for (int q = 0; q < C::BN / 8; ++q) {
-          if (vec)
-            reinterpret_cast<uint4*>(crow)[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-          else if (col0 + 8 * q < G.N)
-            store_piece(crow + 8 * q, make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]),
-                        min(8, G.N - col0 - 8 * q));
-        }
-      }
-    }
-  }
-done:
-  tc::fence_before_sync();
-  __syncthreads();
-  cluster_sync();   // the leader's MMAs read this CTA's shared memory until here
-  if (warp == 1) {
-    tc::fence_after_sync();
-    tc::tmem_dealloc_pair(tmem, C::TMEM_COLS);
-  }
-}
-
-}  // namespace
 
 namespace {
 

@@ -46,7 +46,6 @@ constexpr int kMaxRanks = 8;
 constexpr int kCtaCounter = 16;   // flag-buffer word counting this rank's finished CTAs
 constexpr int kEpochWord = 20;    // flag-buffer word holding the last epoch (device-epoch mode)
 
-__host__ __device__ __forceinline__ int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
 struct GemvArgs {
   const uint8_t* a;
