@@ -24,6 +24,20 @@ def test_oracle_e4m3_rounding(oracle):
     assert oracle.e4m3_rne_satfinite(np.array([1.0625]))[0] == 0x38                  # 1 + 1/16: tie -> even (1.0)
 
 
+def test_oracle_e4m3_matches_torch_cast(oracle):
+    """Independent pin of the oracle's e4m3 rounding: for 200k random finite
+    values inside the e4m3 range, round-to-nearest-even must give the same byte
+    as torch's own float8_e4m3fn cast (which rounds to nearest even; the range
+    is kept inside +-448 because the cast does not saturate)."""
+    rng = np.random.default_rng(1)
+    mag = np.exp2(rng.uniform(-12, np.log2(448.0), 200_000))
+    x = (mag * rng.choice([-1.0, 1.0], mag.size)).astype(np.float32)
+    x[:6] = [0.0, 2.0 ** -9, 2.0 ** -10, 3 * 2.0 ** -10, 448.0, 1.0625]   # ties and edges
+    ours = oracle.e4m3_rne_satfinite(np.abs(x).astype(np.float64)).astype(np.uint8)
+    theirs = torch.from_numpy(np.abs(x)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(ours, theirs)
+
+
 def test_oracle_quantize_roundtrip(pkg, oracle):
     rng = np.random.default_rng(0)
     x = (rng.standard_normal((64, 256)) * 3).astype(np.float16)
