@@ -38,6 +38,23 @@ def test_oracle_e4m3_matches_torch_cast(oracle):
     np.testing.assert_array_equal(ours, theirs)
 
 
+def test_oracle_e2m1_matches_brute_force(oracle):
+    """The e2m1 rounding cross-checked by brute force: nearest of the eight
+    magnitudes by direct distance, ties to the even code, saturation at 6."""
+    rng = np.random.default_rng(2)
+    v = rng.uniform(-8, 8, 100_000)
+    grid = np.array([0, .5, 1, 1.5, 2, 3, 4, 6])
+    v[:16] = np.concatenate([(grid[1:] + grid[:-1]) / 2, [-0.25, 6.5, -7, 0, 5.0, 2.5, 0.75, 1.25, 1.75][:9]])
+    a = np.minimum(np.abs(v), 6.0)
+    d = np.abs(a[:, None] - grid[None, :])
+    best = d.min(axis=1, keepdims=True)
+    cand = np.where(d == best, np.arange(8)[None, :], 99)
+    even = np.where(cand % 2 == 0, cand, 99).min(axis=1)
+    mag = np.where(even < 99, even, cand.min(axis=1))
+    want = (mag | np.where(np.signbit(v), 8, 0)).astype(np.uint8)
+    np.testing.assert_array_equal(oracle.e2m1_rne_satfinite(v), want)
+
+
 def test_oracle_quantize_roundtrip(pkg, oracle):
     rng = np.random.default_rng(0)
     x = (rng.standard_normal((64, 256)) * 3).astype(np.float16)
