@@ -83,16 +83,20 @@ NVFP4_API int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid);
  * into EVERY rank's full-size output buffer peer_out[r] (device pointers valid
  * on this GPU: peer memory over NVLink, e.g. from torch symmetric memory), with
  * element strides c_sm / c_sl.  peer_flags[r] is rank r's flag buffer: at least
- * 32 zero-initialised 32-bit words in memory every rank can reach.  Word 16 of
- * this rank's buffer counts its finished CTAs; the last CTA writes `epoch` into
- * word `rank` of every rank's buffer and waits until this rank's words 0..world-1
- * all hold `epoch`, so the launch ends with every rank's rows present locally.
+ * 64 zero-initialised 32-bit words in memory every rank can reach.  Word 16 of
+ * this rank's buffer counts its finished CTAs (the last one resets it to 0); the
+ * last CTA writes `epoch` into word `rank` of every rank's buffer and waits until
+ * this rank's words 0..world-1 all hold `epoch`, so the launch ends with every
+ * rank's rows present locally.  Words 32-37 of this rank's buffer receive three
+ * 64-bit %globaltimer stamps (low word first): the launch's start, the moment this
+ * rank's rows were all published, and the moment every rank's rows had arrived.
  * `epoch` is the 1-based count of calls made with these flag buffers (the same
  * on every rank; the shape must stay the same between calls).  epoch == 0
  * selects device-epoch mode: the kernel keeps the count in word 20 of this
  * rank's flag buffer, so a captured CUDA graph of the call advances it on every
  * replay (use one mode per set of flag buffers).  The wait is
- * bounded (2 s, error bit 4 in nvfp4_device_errors()).  Requires the aligned
+ * bounded (2 s by default, see nvfp4_set_peer_wait_ns; error bit 16 in
+ * nvfp4_device_errors()).  Requires the aligned
  * (TMA) path; world <= 8.  Replaces "nvfp4_gemv_forward + an output
  * all-gather" (the reference has no distributed code; the north star asks for
  * row sharding with an output all-gather).
@@ -104,6 +108,16 @@ NVFP4_API int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa
                                    void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
                                    uint32_t* const* peer_flags, int world, int rank, uint32_t epoch,
                                    void* stream);
+
+/*
+ * Budget of the fused all-gather's wait for the other ranks' rows, in
+ * nanoseconds, for launches made after the call (process-wide).  0 restores the
+ * default of 2 s; other values must lie in [1e3, 2e9].  A short budget lets a
+ * caller (or a test) detect a rank that never delivers without stalling for the
+ * default.  No counterpart in the reference, whose waits never expire
+ * (blackwell_nvfp4_gemv.cu:150-157).
+ */
+NVFP4_API int nvfp4_set_peer_wait_ns(uint64_t ns);
 
 /*
  * Reads this device's error word (bits set by device-side bounded waits that

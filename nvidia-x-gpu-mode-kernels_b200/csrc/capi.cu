@@ -1,5 +1,6 @@
 // Library-wide C ABI pieces: error messages, version, the per-device error word
 // that bounded waits report into, and the bounded-wait self-test kernel.
+#include <atomic>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -16,7 +17,9 @@ thread_local char g_msg[512] = "";
 __device__ uint32_t g_error_word;
 
 constexpr int kMaxDevices = 64;
-uint32_t* g_err_ptr[kMaxDevices] = {};
+// Per-device addresses, published with release stores and read with acquire
+// loads outside the lock (double-checked initialisation).
+std::atomic<uint32_t*> g_err_ptr[kMaxDevices] = {};
 int g_sms[kMaxDevices] = {};
 std::mutex g_mu;
 
@@ -45,14 +48,14 @@ int fail(int code, const char* fmt, ...) {
 uint32_t* device_error_word() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  if (g_err_ptr[dev]) return g_err_ptr[dev];
+  if (uint32_t* p = g_err_ptr[dev].load(std::memory_order_acquire)) return p;
   std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_err_ptr[dev]) {
+  if (!g_err_ptr[dev].load(std::memory_order_relaxed)) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) return nullptr;
-    g_err_ptr[dev] = static_cast<uint32_t*>(p);
+    g_err_ptr[dev].store(static_cast<uint32_t*>(p), std::memory_order_release);
   }
-  return g_err_ptr[dev];
+  return g_err_ptr[dev].load(std::memory_order_relaxed);
 }
 
 int sm_count() {
@@ -221,7 +224,7 @@ namespace {
 constexpr int kSelftestMaxWaiters = 64;
 static __device__ __align__(256) uint32_t g_selftest_scratch[kSelftestMaxWaiters];
 
-uint32_t* g_selftest_ptr[kMaxDevices] = {};
+std::atomic<uint32_t*> g_selftest_ptr[kMaxDevices] = {};
 
 // Each block waits on its own mbarrier that nothing completes; thread 0
 // records 1 (completed) or 2 (expired) in word blockIdx.x of `outcome`.
@@ -244,16 +247,19 @@ int selftest_scratch(uint32_t** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_UNSUPPORTED, "device index %d out of range", dev);
-  if (!g_selftest_ptr[dev]) {
+  uint32_t* ptr = g_selftest_ptr[dev].load(std::memory_order_acquire);
+  if (!ptr) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_selftest_ptr[dev]) {
+    ptr = g_selftest_ptr[dev].load(std::memory_order_relaxed);
+    if (!ptr) {
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_selftest_scratch);
       if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(self-test scratch)");
-      g_selftest_ptr[dev] = static_cast<uint32_t*>(p);
+      ptr = static_cast<uint32_t*>(p);
+      g_selftest_ptr[dev].store(ptr, std::memory_order_release);
     }
   }
-  *out = g_selftest_ptr[dev];
+  *out = ptr;
   return NVFP4_OK;
 }
 

@@ -29,7 +29,6 @@
 //              the accumulator before storing;
 //   warps 6-9  scale warps: copy each stage's scale blocks from shared memory
 //              into tensor memory with tcgen05.st, each its lane quarter.
-// gemm2_kernel (gemm_pair.cuh) is the CTA-pair variant, kept for the record.
 // Every mbarrier wait is bounded (2 s) and reports into the device error word.
 #include <cuda_fp16.h>
 #include <cstring>
@@ -41,7 +40,6 @@
 
 #include "gemm_cfg.cuh"
 #include "gemm_kernel.cuh"
-#include "gemm_pair.cuh"
 
 namespace nvfp4 {
 
@@ -62,50 +60,6 @@ int launch_gemm(const GemmParams<MAXG>& P, cudaStream_t stream) {
   if (grid < 1) return NVFP4_OK;
   gemm_kernel<C, MAXG><<<grid, C::THREADS, C::SMEM, stream>>>(P);
   return check_launch("gemm_kernel");
-}
-
-template <class C, int MAXG>
-int launch_gemm2(const GemmParams<MAXG>& P, cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  static int max_pairs[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  auto kern = gemm2_kernel<C, MAXG>;
-  cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.blockDim = dim3(C::THREADS);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = stream;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (dev >= 64) return fail(NVFP4_ERR_UNSUPPORTED, "device index out of range");
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(gemm2)");
-    cfg.gridDim = dim3(2 * (sm_count() / 2));
-    int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-    if (e != cudaSuccess || n < 1) return fail(NVFP4_ERR_UNSUPPORTED, "no CTA pairs fit on this device");
-    max_pairs[dev] = n;
-    attr_set[dev] = true;
-  }
-  int pairs = max_pairs[dev];
-  if (P.total_tiles < pairs) pairs = P.total_tiles;
-  if (pairs < 1) return NVFP4_OK;
-  cfg.gridDim = dim3(2 * pairs);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(gemm2)");
-  return check_launch("gemm2_kernel");
-}
-
-template <class C, int MAXG>
-int launch_any(const GemmParams<MAXG>& P, cudaStream_t stream) {
-  if constexpr (C::PAIR) return launch_gemm2<C, MAXG>(P, stream);
-  else return launch_gemm<C, MAXG>(P, stream);
 }
 
 int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, int box_rows) {
@@ -143,15 +97,6 @@ int check_out(void* c, int64_t N, int64_t ldc) {
 
 int vec_ok(const void* c, int64_t ldc) { return aligned16(c) && ldc % 8 == 0; }
 
-// Output map for the TMA-store epilogue: fp16 [M, N], 64-column x 128-row boxes
-// with 128-byte swizzle (the staging tile's layout).
-int out_map(CUtensorMap* m, void* c, int64_t M, int64_t N, int64_t ldc) {
-  const uint64_t dims[2] = {(uint64_t)N, (uint64_t)M};
-  const uint64_t str[1] = {(uint64_t)ldc * 2};
-  const uint32_t box[2] = {64, (uint32_t)BM};
-  return encode_tmap(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, c, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
-}
-
 }  // namespace
 }  // namespace nvfp4
 
@@ -170,28 +115,24 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   GemmParams<1> P;
   std::memset(&P, 0, sizeof(P));
   GemmGroup& G = P.g[0];
-  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::B_BOX)) ||
-      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::B_BOX)))
+  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::BN)) ||
+      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::BN)))
     return rc;
   if ((rc = sf_map(&G.tsa, sfa, M, K, 1, C::KPS)) || (rc = sf_map(&G.tsb, sfb1, N, K, C::NB, C::KPS)) ||
       (rc = sf_map(&G.tsb2, sfb2, N, K, C::NB, C::KPS)))
     return rc;
-  G.sfa = static_cast<const uint8_t*>(sfa);
-  G.sfb = static_cast<const uint8_t*>(sfb1);
-  G.sfb2 = static_cast<const uint8_t*>(sfb2);
   G.c = static_cast<__half*>(c);
   G.ldc = ldc;
   G.vec_ok = vec_ok(c, ldc);
-  G.tma_store = G.vec_ok && out_map(&G.tc, c, M, N, ldc) == NVFP4_OK;
   G.M = (int)M; G.N = (int)N; G.K = (int)K;
-  G.tiles_m = (int)((M + C::TILE_M - 1) / C::TILE_M);
+  G.tiles_m = (int)((M + BM - 1) / BM);
   G.tiles_n = (int)((N + C::BN - 1) / C::BN);
   G.tile_begin = 0;
   P.ngroups = 1;
   P.total_tiles = G.tiles_m * G.tiles_n;
   P.err = device_error_word();
   if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_dual_gemm: cannot resolve the device error word");
-  return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
+  return launch_gemm<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace nvfp4
@@ -201,7 +142,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
                                int64_t ldb, int64_t ldc, void* stream) {
   // two 512-element K stages of 108 KB: half the stage handshakes of four 256-element
   // stages at the same bytes in flight (30.9 vs 33.3 us on the dual workload, same box)
-  return dual_run<GemmCfg<128, true, 2, 0, 1, 0, 0, 1, 1, 0, 2>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb,
+  return dual_run<GemmCfg<128, true, 2, 0, 2>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb,
                                                                    ldc, stream);
 }
 
@@ -222,8 +163,6 @@ int skinny_run(const void* x, const void* w, const void* sfx, const void* sfw, v
   if ((rc = operand_map(&G.ta, w, N, K, ldw, BM)) || (rc = operand_map(&G.tb, x, T, K, ldx, C::BN)) ||
       (rc = sf_map(&G.tsa, sfw, N, K, 1, C::KPS)) || (rc = sf_map(&G.tsb, sfx, T, K, 1, C::KPS)))
     return rc;
-  G.sfa = static_cast<const uint8_t*>(sfw);
-  G.sfb = static_cast<const uint8_t*>(sfx);
   G.c = static_cast<__half*>(out);
   G.ldc = ldo;
   G.M = (int)N;
@@ -235,7 +174,7 @@ int skinny_run(const void* x, const void* w, const void* sfx, const void* sfw, v
   P.total_tiles = G.tiles_m;
   P.err = device_error_word();
   if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_gemm_skinny: cannot resolve the device error word");
-  return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
+  return launch_gemm<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
 template <class C, int MAXG>
@@ -245,10 +184,14 @@ int grouped_launches(const nvfp4_group* groups, int num_groups, void* stream) {
   static GemmParams<MAXG> P;          // large; built under a lock, copied into the launch
   static std::mutex mu;
   std::lock_guard<std::mutex> lk(mu);
-  for (int g0 = 0; g0 < num_groups; g0 += MAXG) {
+  // Groups go into launches of up to MAXG non-empty groups each; `next` is the
+  // first group not yet placed (empty groups are skipped, not counted).
+  int next = 0;
+  while (next < num_groups) {
     std::memset(&P, 0, sizeof(P));
     int tiles = 0, n = 0;
-    for (int i = g0; i < num_groups && n < MAXG; ++i) {
+    int i = next;
+    for (; i < num_groups && n < MAXG; ++i) {
       const nvfp4_group& q = groups[i];
       if (q.M == 0) continue;
       int rc;
@@ -258,28 +201,26 @@ int grouped_launches(const nvfp4_group* groups, int num_groups, void* stream) {
           (rc = check_operand("b", q.b, q.sfb, q.N, q.K, q.ldb)) || (rc = check_out(q.c, q.N, q.ldc)))
         return rc;
       GemmGroup& G = P.g[n];
-      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::B_BOX)))
+      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::BN)))
         return rc;
       if ((rc = sf_map(&G.tsa, q.sfa, q.M, q.K, 1, C::KPS)) || (rc = sf_map(&G.tsb, q.sfb, q.N, q.K, C::NB, C::KPS)))
         return rc;
-      G.sfa = static_cast<const uint8_t*>(q.sfa);
-      G.sfb = static_cast<const uint8_t*>(q.sfb);
       G.c = static_cast<__half*>(q.c);
       G.ldc = q.ldc;
       G.vec_ok = vec_ok(q.c, q.ldc);
-      G.tma_store = G.vec_ok && out_map(&G.tc, q.c, q.M, q.N, q.ldc) == NVFP4_OK;
       G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
-      G.tiles_m = (int)((q.M + C::TILE_M - 1) / C::TILE_M);
+      G.tiles_m = (int)((q.M + BM - 1) / BM);
       G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
       G.tile_begin = tiles;
       tiles += G.tiles_m * G.tiles_n;
       ++n;
     }
+    next = i;
     if (n == 0) continue;
     P.ngroups = n;
     P.total_tiles = tiles;
     P.err = err;
-    int rc = launch_any<C, MAXG>(P, static_cast<cudaStream_t>(stream));
+    int rc = launch_gemm<C, MAXG>(P, static_cast<cudaStream_t>(stream));
     if (rc) return rc;
   }
   return NVFP4_OK;
@@ -297,7 +238,7 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
 }  // namespace nvfp4
 
 extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream) {
-  return grouped_run<GemmCfg<256, false, 4, 0, 1, 0, 0>>(groups, num_groups, stream);
+  return grouped_run<GemmCfg<256, false, 4>>(groups, num_groups, stream);
 }
 
 extern "C" int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, const void* sfw, void* out,
@@ -307,10 +248,10 @@ extern "C" int nvfp4_gemm_skinny(const void* x, const void* w, const void* sfx, 
   // 512-element K stages (32 KB of weights each): half the per-stage handshakes of
   // 256-element stages (13.8 vs 16.3 us at T=16, N=14336, K=4096)
   if (T <= 16)
-    return skinny_run<GemmCfg<16, false, 4, 0, 1, 0, 0, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+    return skinny_run<GemmCfg<16, false, 4, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
   if (T <= 32)
-    return skinny_run<GemmCfg<32, false, 4, 0, 1, 0, 0, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
-  return skinny_run<GemmCfg<64, false, 4, 0, 1, 0, 0, 1, 1, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+    return skinny_run<GemmCfg<32, false, 4, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
+  return skinny_run<GemmCfg<64, false, 4, 1, 2>>(x, w, sfx, sfw, out, T, N, K, ldx, ldw, ldo, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -1,9 +1,52 @@
-// The single-CTA tcgen05 GEMM kernel (dual, grouped and skinny GEMMs; see
-// gemm.cu for the design).  Included by gemm.cu only.
+// The tcgen05 GEMM kernel (dual, grouped and skinny GEMMs; see gemm.cu for
+// the design).  Included by gemm.cu only.
 #pragma once
 
 namespace nvfp4 {
 namespace {
+
+// Issues the MMAs of one stage.  `kb` K-blocks of 64 (KPS on full stages: a
+// compile-time count, so the loop unrolls into straight-line MMA issues; a
+// runtime-bounded loop measured ~25 % slower per stage).  Descriptors advance
+// by whole atoms (A_ATOM / B_ATOM bytes, >> 4) and by 32 bytes (>> 4 = 2) per
+// 64-element slice inside a 128-byte swizzled atom.
+template <class C, int KB>
+__device__ __forceinline__ void issue_stage_mmas(uint32_t tmem, uint64_t da, uint64_t db, uint64_t db2,
+                                                 uint32_t sfa_t, uint32_t sfb_t, uint32_t sfb2_t,
+                                                 uint32_t first_accum) {
+#pragma unroll
+  for (int kk = 0; kk < KB; ++kk) {
+    const uint32_t accum = kk == 0 ? first_accum : 1u;
+    const uint64_t off = (uint64_t)((kk >> 2) * (C::A_ATOM >> 4) + 2 * (kk & 3));
+    const uint64_t offb = (uint64_t)((kk >> 2) * (C::B_ATOM >> 4) + 2 * (kk & 3));
+    tc::mma_mxf4nvf4(tmem, da + off, db + offb, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFB_COLS_PER_KB, accum);
+    if (C::DUAL)
+      tc::mma_mxf4nvf4(tmem + C::BN, da + off, db2 + offb, C::IDESC, sfa_t + 4 * kk,
+                       sfb2_t + kk * C::SFB_COLS_PER_KB, accum);
+  }
+}
+
+// Copies, for this warp's tensor-memory lane quarter, row `lane` of every
+// 512-byte scale block of `kb` K-blocks into 4 consecutive columns each: the
+// image a 32x128b.warpx4 copy would make, without occupying the tensor pipe.
+template <class C, int KB>
+__device__ __forceinline__ void stage_scales(const uint8_t* st, uint32_t sf, int lane) {
+  const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFB_COLS_PER_KB;
+#pragma unroll
+  for (int kk = 0; kk < KB; ++kk) {
+    uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
+    tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
+#pragma unroll
+    for (int nb = 0; nb < C::NB; ++nb) {
+      v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB + nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
+      tc::st_32x32b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
+      if (C::DUAL) {
+        v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB2 + nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
+        tc::st_32x32b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
+      }
+    }
+  }
+}
 
 template <class C, int MAXG>
 __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_constant__ GemmParams<MAXG> P) {
@@ -16,10 +59,10 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
     if (threadIdx.x == 0) atomicOr(P.err, kDevErrTimeoutMma);
     return;
   }
-  const uint32_t bar_full = sbase + C::OFF_BAR;
-  const uint32_t bar_empty = bar_full + 8 * C::STAGES;
-  const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;      // scales in tensor memory (SFST)
-  const uint32_t bar_sff = bar_sfr + 8 * C::STAGES;        // scale boxes landed (SEPSF)
+  const uint32_t bar_full = sbase + C::OFF_BAR;             // operand boxes landed
+  const uint32_t bar_empty = bar_full + 8 * C::STAGES;      // stage consumed by the MMAs
+  const uint32_t bar_sfr = bar_empty + 8 * C::STAGES;       // scales staged in tensor memory
+  const uint32_t bar_sff = bar_sfr + 8 * C::STAGES;         // scale boxes landed
   const uint32_t bar_accf = bar_sff + 8 * C::STAGES;
   const uint32_t bar_acce = bar_accf + 8;
   const uint32_t bar_done = bar_acce + 8;
@@ -54,15 +97,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       for (int i = 0; i < P.ngroups; ++i) {
         prefetch_tmap(&P.g[i].ta);
         prefetch_tmap(&P.g[i].tb);
-        if (C::DUAL) prefetch_tmap(&P.g[i].tb2);
-        if (C::SFTMA) {
-          prefetch_tmap(&P.g[i].tsa);
-          prefetch_tmap(&P.g[i].tsb);
-          if (C::DUAL) prefetch_tmap(&P.g[i].tsb2);
+        prefetch_tmap(&P.g[i].tsa);
+        prefetch_tmap(&P.g[i].tsb);
+        if (C::DUAL) {
+          prefetch_tmap(&P.g[i].tb2);
+          prefetch_tmap(&P.g[i].tsb2);
         }
       }
       const uint64_t pol_a = policy_evict_last();   // A tiles are re-read by every N tile
-      const uint64_t pol_b = C::POL ? policy_evict_normal() : policy_evict_first();
+      const uint64_t pol_b = policy_evict_first();
       uint32_t it = 0;
       for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
@@ -75,24 +118,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           if (!mbar_wait(bar_empty + 8 * s, ((it / C::STAGES) & 1) ^ 1, P.err, kDevErrTimeoutEmpty)) goto done;
           const uint32_t st = sbase + s * C::STAGE_BYTES;
           const uint32_t fb = bar_full + 8 * s;
-          // scale boxes always count in full (blocks past the end read as zeros)
-          const uint32_t sf_bytes = (C::DBG & 16) ? 0 : C::SFA_BYTES + C::SFB_BYTES * (C::DUAL ? 2 : 1);
-          const uint32_t bytes = C::A_BYTES + C::B_BYTES * (C::DUAL ? 2 : 1) + (C::SEPSF ? 0 : sf_bytes);
-          if (C::DBG & 4) {
-            mbar_arrive(fb);
-            if (C::SEPSF) mbar_arrive(bar_sff + 8 * s);
-            continue;
-          }
-          if (C::SEPSF) {   // scales first, on their own barrier
-            const uint32_t sb = bar_sff + 8 * s;
-            mbar_arrive_expect_tx(sb, sf_bytes);
-            if (!(C::DBG & 16)) {
-              tma_load_3d(st + C::OFF_SFA, &G.tsa, sb, 0, C::KPS * ks, mt, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, sb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, sb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-            }
-          }
-          mbar_arrive_expect_tx(fb, bytes);
+          // Scales first, on their own barrier, so the scale warps stage them
+          // while the operand bytes are still in flight.  Boxes always count in
+          // full: blocks past the end of a matrix or of K read as zeros.
+          const uint32_t sb = bar_sff + 8 * s;
+          mbar_arrive_expect_tx(sb, C::SF_BYTES);
+          tma_load_3d(st + C::OFF_SFA, &G.tsa, sb, 0, C::KPS * ks, mt, pol_a);
+          tma_load_3d(st + C::OFF_SFB, &G.tsb, sb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
+          if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, sb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
+          mbar_arrive_expect_tx(fb, C::OP_BYTES);
 #pragma unroll
           for (int a = 0; a < C::KA; ++a) {   // atoms past K read as zeros (and count in full)
             const int x = (ks * C::KA + a) * KSTEP_BYTES;
@@ -100,21 +134,15 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             tma_load_2d(st + C::OFF_B + a * C::B_ATOM, &G.tb, fb, x, nt * C::BN, pol_b);
             if (C::DUAL) tma_load_2d(st + C::OFF_B2 + a * C::B_ATOM, &G.tb2, fb, x, nt * C::BN, pol_b);
           }
-          if (!(C::DBG & 16) && !C::SEPSF) {
-            if (C::SFTMA) {
-              tma_load_3d(st + C::OFF_SFA, &G.tsa, fb, 0, C::KPS * ks, mt, pol_a);
-              tma_load_3d(st + C::OFF_SFB, &G.tsb, fb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-              if (C::DUAL) tma_load_3d(st + C::OFF_SFB2, &G.tsb2, fb, 0, C::KPS * ks, (nt * C::BN) / 128, pol_b);
-            } else {
-              load_sf_bulk<C>(st, G, mt, (nt * C::BN) / 128, nk64, ks, fb);
-            }
-          }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------ MMA -------------------------------
     if (lane == 0) {
+      const uint64_t da0 = tc::desc_sw128(sbase);
+      const uint64_t db0 = tc::desc_sw128(sbase + C::OFF_B);
+      const uint64_t db20 = tc::desc_sw128(sbase + C::OFF_B2);
       uint32_t it = 0, tile_it = 0;
       for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x, ++tile_it) {
         const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
@@ -127,36 +155,29 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
         tc::fence_after_sync();
         for (int ks = 0; ks < nks; ++ks, ++it) {
           const int s = it % C::STAGES;
-          if (!mbar_wait((C::SFST ? bar_sfr : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull))
-            goto done;
-          if (C::SEPSF && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) goto done;
+          const uint32_t par = (it / C::STAGES) & 1;
+          if (!mbar_wait(bar_sfr + 8 * s, par, P.err, kDevErrTimeoutFull)) goto done;
+          if (!mbar_wait(bar_full + 8 * s, par, P.err, kDevErrTimeoutFull)) goto done;
           tc::fence_after_sync();
-          const uint32_t st = sbase + s * C::STAGE_BYTES;
-          const int nch = min(C::KPS, nk64 - C::KPS * ks);
+          const uint64_t soff = (uint64_t)((s * C::STAGE_BYTES) >> 4);
           const uint32_t sf = tmem + C::SF_BASE + s * C::SF_STAGE_COLS;
-          const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFB_COLS_PER_KB;
-          for (int kk = 0; kk < nch && !(C::DBG & 1) && !C::SFST; ++kk) {
-            tc::cp_sf_32x128b_x4(sfa_t + 4 * kk, tc::desc_sf_block(st + C::OFF_SFA + kk * 512));
-            for (int nb = 0; nb < C::NB; ++nb) {
-              tc::cp_sf_32x128b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
-                                   tc::desc_sf_block(st + C::OFF_SFB + nb * C::SFB_ROWTILE + kk * 512));
+          const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS + sfb_off;
+          const uint32_t sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFB_COLS_PER_KB + sfb_off;
+          const uint32_t first = ks > 0 ? 1u : 0u;
+          const int nch = min(C::KPS, nk64 - C::KPS * ks);
+          if (nch == C::KPS) {
+            issue_stage_mmas<C, C::KPS>(tmem, da0 + soff, db0 + soff, db20 + soff, sfa_t, sfb_t, sfb2_t, first);
+          } else {
+            // the last stage of a K that is not a multiple of the stage width
+            for (int kk = 0; kk < nch; ++kk) {
+              const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+              const uint64_t off = soff + (uint64_t)((kk >> 2) * (C::A_ATOM >> 4) + 2 * (kk & 3));
+              const uint64_t offb = soff + (uint64_t)((kk >> 2) * (C::B_ATOM >> 4) + 2 * (kk & 3));
+              tc::mma_mxf4nvf4(tmem, da0 + off, db0 + offb, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFB_COLS_PER_KB,
+                               accum);
               if (C::DUAL)
-                tc::cp_sf_32x128b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb,
-                                     tc::desc_sf_block(st + C::OFF_SFB2 + nb * C::SFB_ROWTILE + kk * 512));
-            }
-          }
-          for (int kk = 0; kk < nch && !(C::DBG & 2); ++kk) {
-            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-            // atom kk / 4 of the stage; its (kk % 4)-th 64-element slice starts
-            // 32 bytes further (encoded >> 4)
-            const int at = kk >> 2, sl = kk & 3;
-            const uint64_t da = tc::desc_sw128(st + at * C::A_ATOM) + 2 * sl;
-            const uint64_t db = tc::desc_sw128(st + C::OFF_B + at * C::B_ATOM) + 2 * sl;
-            tc::mma_mxf4nvf4(tmem, da, db, C::IDESC, sfa_t + 4 * kk, sfb_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
-            if (C::DUAL) {
-              const uint64_t db2 = tc::desc_sw128(st + C::OFF_B2 + at * C::B_ATOM) + 2 * sl;
-              tc::mma_mxf4nvf4(tmem + C::BN, da, db2, C::IDESC, sfa_t + 4 * kk,
-                               sfb2_t + kk * C::SFB_COLS_PER_KB + sfb_off, accum);
+                tc::mma_mxf4nvf4(tmem + C::BN, da0 + off, db20 + offb, C::IDESC, sfa_t + 4 * kk,
+                                 sfb2_t + kk * C::SFB_COLS_PER_KB, accum);
             }
           }
           tc::commit(bar_empty + 8 * s);
@@ -165,46 +186,34 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
       }
     }
   } else if (warp >= 6) {
-    // ------------------- scale warps (SFST == 1 only) -------------------
-    // Each warp copies, for its tensor-memory lane quarter, the 16 bytes of
-    // every 512-byte scale block of the stage (row `lane` of the block) into 4
-    // consecutive columns: the same image a 32x128b.warpx4 copy would make.
+    // --------------------------- scale warps ---------------------------
+    // Each warp copies the stage's scale blocks into its tensor-memory lane
+    // quarter (the MMA reads every quarter).  Issuing the same copies as
+    // tcgen05.cp from the MMA thread serialises them with the MMAs on the
+    // tensor pipe (~23 ns each, 12 per stage).
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint32_t it = 0;
     bool dead = false;
-    for (int t = blockIdx.x; t < P.total_tiles; t += gridDim.x) {
+    for (int t = blockIdx.x; t < P.total_tiles && !dead; t += gridDim.x) {
       const GemmGroup& G = P.g[find_group(P.g, P.ngroups, t)];
       const int nk64 = G.K / 64;
       const int nks = (nk64 + C::KPS - 1) / C::KPS;
       for (int ks = 0; ks < nks; ++ks, ++it) {
         const int s = it % C::STAGES;
-        if (!dead && !mbar_wait((C::SEPSF ? bar_sff : bar_full) + 8 * s, (it / C::STAGES) & 1, P.err,
-                                kDevErrTimeoutFull))
+        if (!mbar_wait(bar_sff + 8 * s, (it / C::STAGES) & 1, P.err, kDevErrTimeoutFull)) {
           dead = true;
-        if (dead) break;
-        const uint8_t* st = smem_raw + (sbase - raw) + s * C::STAGE_BYTES;
-        const int nch = min(C::KPS, nk64 - C::KPS * ks);
-        const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
-        const uint32_t sfa_t = sf, sfb_t = sf + C::SFA_COLS, sfb2_t = sf + C::SFA_COLS + C::KPS * C::SFB_COLS_PER_KB;
-        for (int kk = 0; kk < nch && !(C::DBG & 1); ++kk) {
-          uint4 v = *reinterpret_cast<const uint4*>(st + C::OFF_SFA + kk * 512 + lane * 16);
-          tc::st_32x32b_x4(sfa_t + 4 * kk, v.x, v.y, v.z, v.w);
-#pragma unroll
-          for (int nb = 0; nb < C::NB; ++nb) {
-            v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB + nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
-            tc::st_32x32b_x4(sfb_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
-            if (C::DUAL) {
-              v = *reinterpret_cast<const uint4*>(st + C::OFF_SFB2 + nb * C::SFB_ROWTILE + kk * 512 + lane * 16);
-              tc::st_32x32b_x4(sfb2_t + kk * C::SFB_COLS_PER_KB + 4 * nb, v.x, v.y, v.z, v.w);
-            }
-          }
+          break;
         }
+        const uint8_t* st = smem_raw + (sbase - raw) + s * C::STAGE_BYTES;
+        const uint32_t sf = tmem + lane_base + C::SF_BASE + s * C::SF_STAGE_COLS;
+        // on a last, partial stage the blocks past K arrived as zeros (the
+        // box reads past the end as zeros) and no MMA reads them
+        stage_scales<C, C::KPS>(st, sf, lane);
         tc::wait_st();
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_sfr + 8 * s);
       }
-      if (dead) break;
     }
   } else {
     // ---------------------------- epilogue ----------------------------
@@ -243,17 +252,12 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             }
           }
         }
-        continue;
-      }
-      if (!(C::EPI && G.tma_store) && !(C::DBG & 8) && !C::DUAL) {
+      } else if constexpr (!C::DUAL) {
         // Drain the whole accumulator row into registers (packed fp16) and
         // release it before storing anything, so the next tile's MMAs run while
         // this tile's global stores drain.  Storing chunk by chunk between the
         // tensor-memory loads held the accumulator ~3 us per tile (the 16-byte
-        // row-strided stores are slow to issue).  The dual GEMM keeps the
-        // chunked order below: with ~1.5 tiles per CTA its last epilogue is on
-        // the critical path, where interleaving loads and stores is shorter
-        // (31.7 vs 33.4 us on the dual workload; 74.1 vs 74.9 grouped).
+        // row-strided stores are slow to issue).
         uint32_t h[C::BN / 2];
 #pragma unroll
         for (int cb = 0; cb < C::BN / 16; ++cb) {   // 16 columns per load keeps the live set small
@@ -280,21 +284,16 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
             }
           }
         }
-        continue;
-      }
-      if (C::EPI && G.tma_store) {
-        // previous tile's TMA stores must have finished reading the staging tile
-        if (threadIdx.x == 64) bulk_wait_read_all();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-      }
-      __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
+      } else {
+        // Dual GEMM: 32 columns of both accumulators at a time, SiLU gate,
+        // stores interleaved with the loads.  With ~1.5 tiles per CTA the last
+        // epilogue is on the critical path, where interleaving is shorter than
+        // draining first (31.7 vs 33.4 us on the dual workload).
+        __half* crow = G.c + (int64_t)row * G.ldc + (int64_t)nt * C::BN;
 #pragma unroll 1
-      for (int cb = 0; cb < C::BN / 32 && !(C::DBG & 8); ++cb) {
-        uint32_t v[32];
-        tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
-        uint32_t h[16];
-        if constexpr (C::DUAL) {
-          uint32_t u[32];
+        for (int cb = 0; cb < C::BN / 32; ++cb) {
+          uint32_t v[32], u[32], h[16];
+          tc::ld_32x32b_x32(tmem + lane_base + cb * 32, v);
           tc::ld_32x32b_x32(tmem + lane_base + C::BN + cb * 32, u);
           tc::wait_ld();
           if (cb == C::BN / 32 - 1) {   // accumulator fully read: let the next tile's MMAs start
@@ -306,54 +305,20 @@ __global__ void __launch_bounds__(C::THREADS, 1) gemm_kernel(const __grid_consta
           for (int j = 0; j < 16; ++j)
             h[j] = pack_h2(silu_mul(__uint_as_float(v[2 * j]), __uint_as_float(u[2 * j])),
                            silu_mul(__uint_as_float(v[2 * j + 1]), __uint_as_float(u[2 * j + 1])));
-        } else {
-          tc::wait_ld();
-          if (cb == C::BN / 32 - 1) {
-            tc::fence_before_sync();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_acce);
-          }
+          const int col0 = nt * C::BN + cb * 32;
+          if (row < G.M) {
+            if (col0 + 32 <= G.N && G.vec_ok) {
+              uint4* dst = reinterpret_cast<uint4*>(crow + cb * 32);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) h[j] = pack_h2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-        }
-        if (C::EPI && G.tma_store) {
-          // box cb/2 holds 64 columns: row rloc at 128 * rloc, 16-byte chunk q at (q ^ (rloc % 8))
-          uint8_t* box = smem_raw + C::OFF_C + (cb >> 1) * (BM * 128) + rloc * 128;
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int chunk = ((cb & 1) * 4 + q) ^ (rloc & 7);
-            *reinterpret_cast<uint4*>(box + chunk * 16) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+              for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+            } else {
+              const __half* hs = reinterpret_cast<const __half*>(h);
+              for (int j = 0; j < 32 && col0 + j < G.N; ++j) crow[cb * 32 + j] = hs[j];
+            }
           }
-          continue;
-        }
-        const int col0 = nt * C::BN + cb * 32;
-        if (row < G.M) {
-          if (col0 + 32 <= G.N && G.vec_ok) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + cb * 32);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-          } else {
-            const __half* hs = reinterpret_cast<const __half*>(h);
-            for (int j = 0; j < 32 && col0 + j < G.N; ++j) crow[cb * 32 + j] = hs[j];
-          }
-        }
-      }
-      if (C::DBG & 8) {
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar_acce);
-      }
-      if (C::EPI && G.tma_store && !(C::DBG & 8)) {
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (threadIdx.x == 64) {
-          for (int b = 0; b < C::BN / 64; ++b)
-            tma_store_2d(&G.tc, sbase + C::OFF_C + b * (BM * 128), nt * C::BN + 64 * b, mt * BM);
-          bulk_commit_group();
         }
       }
     }
-    if (threadIdx.x == 64) bulk_wait_all();
   }
 done:
   tc::fence_before_sync();

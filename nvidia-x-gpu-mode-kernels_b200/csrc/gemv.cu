@@ -34,6 +34,7 @@
 // Every wait is bounded (2 s) and reports into the device error word.
 #include <cuda_fp16.h>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include "ptx.cuh"
 #include "common.h"
@@ -43,8 +44,9 @@ namespace nvfp4 {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kCtaCounter = 16;   // flag-buffer word counting this rank's finished CTAs
+constexpr int kCtaCounter = 16;   // flag-buffer word counting this rank's finished CTAs (reset per call)
 constexpr int kEpochWord = 20;    // flag-buffer word holding the last epoch (device-epoch mode)
+constexpr int kStampWord = 32;    // words 32-37: %globaltimer at start / rows published / all peers seen
 
 
 struct GemvArgs {
@@ -65,7 +67,7 @@ struct GemvArgs {
   int64_t m_off;
   uint32_t epoch;    // 1-based call count of this gather (same on every rank)
   int vec_rows;      // c_sm == 1 and 16-byte aligned row runs: whole-piece peer stores
-  int dbg;           // tuning only (0 in the product): 1 no peer stores, 2 no wait, 4 no epoch stores, 8 timestamps
+  uint64_t peer_wait_ns;   // budget of the wait for the other ranks' rows
 };
 
 struct GemvMaps {
@@ -73,16 +75,13 @@ struct GemvMaps {
 };
 
 // ROWS rows x KTB A-bytes per stage; CW consumer warps; MINB CTAs per SM.
-// MODE 0 computes; MODE 1 only streams (consumers release stages untouched) and
-// exists to measure the copy pipeline's ceiling during tuning.
-template <int ROWS_, int KTB_, int STAGES_, int CW_, int MINB_ = 1, int MODE_ = 0>
+template <int ROWS_, int KTB_, int STAGES_, int CW_, int MINB_ = 1>
 struct GemvCfg {
   static constexpr int ROWS = ROWS_;
   static constexpr int KTB = KTB_;
   static constexpr int STAGES = STAGES_;
   static constexpr int CW = CW_;
   static constexpr int MINB = MINB_;
-  static constexpr int MODE = MODE_;
   static constexpr int THREADS = (CW + 1) * 32;
   static constexpr int NCH = KTB / 512;          // 512-byte column chunks per row
   static constexpr int GROUPS = CW / NCH;        // row groups
@@ -169,10 +168,10 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
   if (p.world > 0 && p.epoch == 0 && threadIdx.x == 0)
     epoch_at_start = *reinterpret_cast<volatile uint32_t*>(p.peer_flag[p.rank] + kEpochWord) + 1u;
 
-  if ((p.dbg & 8) && p.world > 0 && blockIdx.x == 0 && threadIdx.x == 0) {
-    const uint64_t t = globaltimer();   // tuning only: flag words 32-37 hold start / signal / done times
-    p.peer_flag[p.rank][32] = (uint32_t)t;
-    p.peer_flag[p.rank][33] = (uint32_t)(t >> 32);
+  if (p.world > 0 && blockIdx.x == 0 && threadIdx.x == 0) {
+    const uint64_t t = globaltimer();
+    p.peer_flag[p.rank][kStampWord] = (uint32_t)t;
+    p.peer_flag[p.rank][kStampWord + 1] = (uint32_t)(t >> 32);
   }
   const int64_t M = p.M;
   const int nk = (int)((p.K / 2 + C::KTB - 1) / C::KTB);
@@ -228,7 +227,7 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
       const int s = it % C::STAGES;
       if (!dead && !mbar_wait(bar_full + 8 * s, (it / C::STAGES) & 1, p.err, kDevErrTimeoutFull)) dead = true;
       const uint8_t* st = smem + s * C::STAGE_BYTES;
-      if constexpr (C::MODE == 0) {
+      {
         uint32_t bh[16];
         float sb0, sb1;
         {
@@ -264,7 +263,7 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
     // fused gather with contiguous output rows: stage the tile's results and
     // send each peer whole 16-byte pieces instead of one 2-byte store per row
-    const bool vec = (C::ROWS % 8 == 0) && p.world > 0 && !(p.dbg & 1) && p.vec_rows && m0 + C::ROWS <= M;
+    const bool vec = (C::ROWS % 8 == 0) && p.world > 0 && p.vec_rows && m0 + C::ROWS <= M;
     __half* hb = reinterpret_cast<__half*>(smem + C::OFF_HB) + parity * C::ROWS;
     for (int row = threadIdx.x; row < C::ROWS; row += C::CW * 32) {
       float v = 0.f;
@@ -278,8 +277,7 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
           p.c[l * p.c_sl + (m0 + row) * p.c_sm] = hv;
         } else {
           const int64_t off = l * p.c_sl + (p.m_off + m0 + row) * p.c_sm;
-          if (p.dbg & 1) p.c[off] = hv;
-          else for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
+          for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
         }
       }
     }
@@ -298,9 +296,10 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
     // Completion, two levels.  Each CTA counts itself into this rank's local
     // counter (word kCtaCounter of its flag buffer); the CTA that completes the
     // count is last on this GPU, so every row of this rank has been stored: it
-    // publishes them (system fence) and writes the call's epoch into word
-    // `rank` of every rank's flag buffer, then waits until every rank's word
-    // holds this epoch, i.e. all rows of all ranks have landed here.
+    // resets the counter for the next call, publishes the rows (system fence)
+    // and writes the call's epoch into word `rank` of every rank's flag buffer,
+    // then waits until every rank's word holds this epoch, i.e. all rows of all
+    // ranks have landed here.  Words kStampWord.. record when each step happened.
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
     if (threadIdx.x == 0) {
       // epoch 0 = device-epoch mode: this launch is number (stored + 1).  Every
@@ -312,36 +311,32 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
       __threadfence_system();
       uint32_t* mine = p.peer_flag[p.rank];
       const uint32_t done = atomicAdd(mine + kCtaCounter, 1u) + 1u;
-      if (done == epoch * gridDim.x) {
+      if (done == gridDim.x) {
+        mine[kCtaCounter] = 0u;   // every CTA of this launch has counted in
         __threadfence_system();
-        if (p.dbg & 8) {
-          const uint64_t t = globaltimer();
-          mine[34] = (uint32_t)t;
-          mine[35] = (uint32_t)(t >> 32);
-        }
-        if (!(p.dbg & 4))
-          for (int r = 0; r < p.world; ++r)
-            // relaxed: the system fence above already orders every row store
-            // before these; a release per store would fence (and wait) per peer
-            asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(epoch)
-                         : "memory");
+        const uint64_t ts = globaltimer();
+        mine[kStampWord + 2] = (uint32_t)ts;
+        mine[kStampWord + 3] = (uint32_t)(ts >> 32);
+        for (int r = 0; r < p.world; ++r)
+          // relaxed: the system fence above already orders every row store
+          // before these; a release per store would fence (and wait) per peer
+          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(epoch)
+                       : "memory");
         const uint64_t t0 = globaltimer();
-        for (int r = 0; r < p.world && !(p.dbg & 2); ++r) {
+        for (int r = 0; r < p.world; ++r) {
           for (uint32_t it = 0;; ++it) {
             uint32_t v;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
             if ((int32_t)(v - epoch) >= 0) break;
-            if ((it & 63u) == 63u && globaltimer() - t0 > kWaitBudgetNs) {
+            if ((it & 63u) == 63u && globaltimer() - t0 > p.peer_wait_ns) {
               atomicOr(p.err, kDevErrTimeoutPeer);
               break;
             }
           }
         }
-        if (p.dbg & 8) {
-          const uint64_t t = globaltimer();
-          mine[36] = (uint32_t)t;
-          mine[37] = (uint32_t)(t >> 32);
-        }
+        const uint64_t te = globaltimer();
+        mine[kStampWord + 4] = (uint32_t)te;
+        mine[kStampWord + 5] = (uint32_t)(te >> 32);
         if (p.epoch == 0) mine[kEpochWord] = epoch;
         __threadfence_system();
       }
@@ -598,7 +593,21 @@ extern "C" int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid) {
   return gemv_dispatch(args, nullptr, grid);
 }
 
-static int g_gather_dbg = 0;   // set only by tuning probes that compile this file in
+namespace nvfp4 {
+namespace {
+std::atomic<uint64_t> g_peer_wait_ns{kWaitBudgetNs};
+}
+}  // namespace nvfp4
+
+extern "C" int nvfp4_set_peer_wait_ns(uint64_t ns) {
+  using namespace nvfp4;
+  if (ns == 0) ns = kWaitBudgetNs;
+  if (ns < 1000ull || ns > kWaitBudgetNs)
+    return fail(NVFP4_ERR_INVALID, "nvfp4_set_peer_wait_ns: budget must be 0 (default) or 1e3..2e9 ns, got %llu",
+                (unsigned long long)ns);
+  g_peer_wait_ns.store(ns, std::memory_order_relaxed);
+  return NVFP4_OK;
+}
 
 extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
                                     int64_t M_local, int64_t K, int64_t L, int64_t a_sm, int64_t a_sl,
@@ -641,6 +650,6 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
   bool vec = c_sm == 1 && m_off % 8 == 0 && (L == 1 || c_sl % 8 == 0);
   for (int r = 0; r < world; ++r) vec = vec && aligned16(peer_out[r]);
   args.vec_rows = vec ? 1 : 0;
-  args.dbg = g_gather_dbg;
+  args.peer_wait_ns = g_peer_wait_ns.load(std::memory_order_relaxed);
   return gemv_dispatch(args, static_cast<cudaStream_t>(stream));
 }

@@ -1,5 +1,5 @@
 // Inline-PTX primitives for sm_100a shared by the NVFP4 kernels:
-// mbarriers with bounded waits, 1-D bulk (TMA) copies, tensor-map TMA loads,
+// mbarriers with bounded waits, tensor-map TMA loads, numeric conversions,
 // and the device-side error word every bounded wait reports into.
 #pragma once
 #include <cstdint>
@@ -52,23 +52,15 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(bar) : "memory");
 }
 
-// NVFP4_WAIT_TEST_SPIN (tuning builds only) polls with the non-blocking
-// test_wait instead of the potentially-suspending try_wait.
+// Non-blocking-to-the-caller probe of a phase (try_wait may suspend the
+// thread briefly until the phase completes).
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-#ifdef NVFP4_WAIT_TEST_SPIN
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-#else
   asm volatile(
       "{\n .reg .pred p;\n"
       " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-#endif
   return ok != 0;
 }
 
@@ -88,99 +80,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
   }
 }
 
-// ---- thread-block clusters ------------------------------------------------
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %nclusterid.x;" : "=r"(r));
-  return r;
-}
-// Shared::cluster address of the same shared-memory offset in CTA `rank`.
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Arrive on an mbarrier that may live in another CTA of the cluster (a
-// shared::cluster address from mapa), with the instruction's default
-// semantics, as cluster pipelines conventionally do; the explicit
-// .release.cluster form measured as a full memory barrier per arrival.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" :: "r"(cluster_addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-  return ok != 0;
-}
-// Bounded wait with cluster-scope acquire (arrivals from the peer CTA).
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, uint32_t* err, uint32_t err_bit,
-                                                  uint64_t budget_ns = kWaitBudgetNs) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 15u) == 15u && globaltimer() - t0 > budget_ns) {
-      if (err) atomicOr(err, err_bit);
-      return false;
-    }
-  }
-}
-
-// 2-D tensor TMA load for a CTA pair: lands in this CTA's shared memory and
-// completes transaction bytes on the mbarrier at `bar_cluster` (the pair
-// leader's barrier).  No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster, int x, int y,
-                                                 uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-      "[%0], [%1, {%3, %4}], [%2], %5;"
-      :: "r"(dst), "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy) : "memory");
-}
-
-// 1-D bulk copy global -> shared (the TMA unit's non-tensor form); completion
-// is reported as transaction bytes on `bar`.  Both addresses 16-byte aligned,
-// size a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
-                                         uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes,
-                                              uint32_t bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-      "[%0], [%1], %2, [%3], %4;"
-      :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
-}
-
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
-__device__ __forceinline__ uint64_t policy_evict_normal() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 
@@ -206,17 +108,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       "[%0], [%1, {%3, %4, %5}], [%2], %6;"
       :: "r"(dst), "l"(tmap), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(policy) : "memory");
 }
-
-// Tensor-map TMA store shared -> global (bulk-group completion).
-__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {
-  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
-               :: "l"(tmap), "r"(src), "r"(x), "r"(y) : "memory");
-}
-__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Wait until the committed bulk stores no longer read shared memory.
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-// Wait until the committed bulk stores are complete.
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
@@ -265,14 +156,6 @@ __device__ __forceinline__ uint32_t hadd2(uint32_t a, uint32_t b) {
 __device__ __forceinline__ void h2_to_f2(uint32_t h, float& lo, float& hi) {
   asm("{\n .reg .f16 l, h;\n mov.b32 {l, h}, %2;\n cvt.f32.f16 %0, l;\n cvt.f32.f16 %1, h;\n}\n"
       : "=f"(lo), "=f"(hi) : "r"(h));
-}
-
-// Sum of the two halves of an f16x2, in f16, widened to f32.
-__device__ __forceinline__ float h2_hsum_f32(uint32_t h) {
-  float r;
-  asm("{\n .reg .f16 l, h, s;\n mov.b32 {l, h}, %1;\n add.rn.f16 s, l, h;\n cvt.f32.f16 %0, s;\n}\n"
-      : "=f"(r) : "r"(h));
-  return r;
 }
 
 }  // namespace nvfp4
