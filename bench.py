@@ -4,9 +4,16 @@
 
 Headline workload (N = 1): config 1, the large single-vector GEMV
 M = K = 16384, L = 1.  For N > 1 (torchrun, one rank per GPU) the same problem
-is row-sharded across ranks and the fp16 output is all-gathered with NCCL
-(strong scaling: total work fixed).  ``value`` is HBM GB/s of algorithmic
-bytes (whole job); ``ms_per_step`` the device time of one step.
+is row-sharded across ranks and the fp16 output is all-gathered inside the
+kernel by NVLink peer stores (strong scaling: total work fixed); the plain
+kernel + NCCL all-gather is timed beside it, and config 4 (the grouped GEMM)
+runs group-sharded with one padded NCCL all-gather.  ``value`` is HBM GB/s of
+algorithmic bytes (whole job); ``ms_per_step`` the device time of one step.
+
+Before timing, every rank checks its result: at N = 1 against the CPU oracle
+on a row sample (contract tolerance), at N > 1 bit for bit against the
+single-GPU kernel's output on the full problem.  A mismatch on any rank makes
+every rank exit non-zero.
 
 Timing: W untimed warm-up steps; then K steps, each bracketed by CUDA events on
 the launching stream, with a 512 MiB L2 flush (outside the events) before each
@@ -201,6 +208,23 @@ def oracle_mod():
     return nvfp4_oracle
 
 
+def cpu_time(fn, target_s):
+    """Seconds per call of fn, over as many calls as fit in ~target_s (>= 1)."""
+    t0 = time.perf_counter()
+    fn()
+    one = time.perf_counter() - t0
+    reps = max(1, int(target_s / max(one, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn()
+    return (time.perf_counter() - t0) / reps, reps
+
+
+def cpu_baseline(value, unit, sample):
+    return {"value": round(value, 4), "unit": unit, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": sample, "host_cpus": os.cpu_count()}
+
+
 def cpu_gemv_sample(pkg, M, K, L, target_s=10.0, max_rows=2048):
     """Times the CPU restatement (torch, all threads) on a row sample of the
     workload; returns (GB/s of algorithmic bytes, sample description, threads)."""
@@ -366,6 +390,134 @@ def run_quant_extra(pkg, flush, steps, warmup, hbm, M=8192, K=7168):
             "gbs": round(nbytes / t / 1e9, 1), "hbm_frac": round(nbytes / t / 1e9 / hbm, 4)}
 
 
+def all_ok(world, ok: bool) -> bool:
+    """True when every rank passed."""
+    t = torch.tensor([0.0 if ok else 1.0], device="cuda")
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item() == 0.0
+
+
+def gather_rows(world, values):
+    """All ranks' lists of floats, on every rank (rank order)."""
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    if world == 1:
+        return [t.tolist()]
+    import torch.distributed as dist
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [o.tolist() for o in out]
+
+
+def gather_stamps(fused, step, world, n=20):
+    """Per-rank medians over n synchronised calls of the fused gather's
+    %globaltimer stamps: own rows published and all ranks' rows present, in us
+    after the rank's launch began, plus each rank's start relative to the
+    earliest (GPU timers of one node; offsets between them are not removed)."""
+    pub, seen, starts = [], [], []
+    for _ in range(n):
+        step([])
+        torch.cuda.synchronize()
+        w = fused.flags[32:38].cpu().numpy().view("uint32").astype("uint64")
+        t0, t1, t2 = (int(w[2 * i]) | (int(w[2 * i + 1]) << 32) for i in range(3))
+        pub.append((t1 - t0) / 1e3)
+        seen.append((t2 - t0) / 1e3)
+        starts.append(float(t0))
+    rows = gather_rows(world, [statistics.median(pub), statistics.median(seen)] + starts)
+    first = [min(r[2 + i] for r in rows) for i in range(n)]
+    return [{"rank": r, "rows_published_us": round(v[0], 2), "all_rows_present_us": round(v[1], 2),
+             "start_after_first_rank_us": round(statistics.median((v[2 + i] - first[i]) / 1e3 for i in range(n)), 2)}
+            for r, v in enumerate(rows)]
+
+
+def run_grouped_sharded_extra(pkg, flush, steps, warmup, world, align, peak_tf):
+    """Config 4 with its groups LPT-assigned to ranks: one grouped launch per
+    rank over its own groups, one padded NCCL all-gather of the outputs.
+    Checked bit for bit against the single-GPU grouped GEMM on every rank."""
+    N, K = 4096, 7168
+    Ms = pkg.inputs.grouped_m_sizes(8, seed=0)
+    g = torch.Generator().manual_seed(0)
+    As = [pkg.inputs.operand(m, K, g, device="cuda") for m in Ms]
+    Bs = [pkg.inputs.operand(N, K, g, device="cuda") for _ in Ms]
+    ref = [torch.empty((m, N), dtype=torch.float16, device="cuda") for m in Ms]
+    pkg.grouped_gemm([a.codes for a in As], [b.codes for b in Bs], [a.sf_blocked for a in As],
+                     [b.sf_blocked for b in Bs], ref)
+    sh = pkg.sharded.ShardedGroupedGemm(Ms, N, K)
+    mine = sh.mine
+    args = ([As[i].codes for i in mine], [Bs[i].codes for i in mine], [As[i].sf_blocked for i in mine],
+            [Bs[i].sf_blocked for i in mine])
+    sh(pkg.grouped_gemm, *args)
+    torch.cuda.synchronize()
+    diff = max(float((o.float() - r.float()).abs().max()) for o, r in zip(sh.outputs(), ref))
+    ok = all(torch.equal(o, r) for o, r in zip(sh.outputs(), ref))
+
+    def step(ev):
+        ev_mark(ev)
+        sh(pkg.grouped_gemm, *args)
+        ev_mark(ev)
+
+    t_ms = statistics.mean(s[0] for s in time_steps(step, steps, warmup, flush, align=align))
+    (t_ms,) = max_over_ranks(world, [t_ms])
+    flop = 2 * sum(Ms) * N * K
+    tf = flop / (t_ms * 1e-3) / 1e12
+    return ok, {"workload": f"grouped gemm G=8 M={Ms} N={N} K={K}, groups LPT-sharded x{world}, "
+                            "one padded NCCL all-gather of the outputs",
+                "us": round(t_ms * 1e3, 3), "tflops": round(tf, 1),
+                "fp4_peak_frac": round(tf / (world * peak_tf), 4),
+                "groups_per_rank": [[i for i, o in enumerate(sh.owner) if o == r] for r in range(world)],
+                "parity": "ok" if ok else "MISMATCH", "max_abs_diff_vs_single_gpu": diff}
+
+
+def cpu_dual(pkg, rows=16, N=14336, K=4096):
+    """CPU restatement of the dual GEMM on `rows` of the 256 tokens (full W1, W2)."""
+    oracle = oracle_mod()
+    g = torch.Generator().manual_seed(0)
+    x, w1, w2 = (pkg.inputs.operand(r, K, g) for r in (rows, N, N))
+    dt, reps = cpu_time(lambda: oracle.dual_gemm_torch(x.codes, w1.codes, w2.codes, x.sf_blocked, w1.sf_blocked,
+                                                       w2.sf_blocked, rows, N, K), 3.0)
+    return cpu_baseline(2 * 2 * rows * N * K / dt / 1e12, "TFLOP/s",
+                        f"{rows} of 256 token rows x N={N} x K={K} (dequantise + fp32 matmul), {reps} reps")
+
+
+def cpu_grouped(pkg, N=4096, K=7168):
+    """CPU restatement of the grouped GEMM on one group (M = 64) of config 4."""
+    oracle = oracle_mod()
+    g = torch.Generator().manual_seed(0)
+    a, b = pkg.inputs.operand(64, K, g), pkg.inputs.operand(N, K, g)
+    dt, reps = cpu_time(lambda: oracle.gemm_torch(a.codes, b.codes, a.sf_blocked, b.sf_blocked, 64, N, K), 3.0)
+    return cpu_baseline(2 * 64 * N * K / dt / 1e12, "TFLOP/s",
+                        f"one group of config 4 (M=64, N={N}, K={K}), {reps} reps")
+
+
+def cpu_skinny(pkg, T=16, N=14336, K=4096):
+    oracle = oracle_mod()
+    g = torch.Generator().manual_seed(0)
+    x, w = pkg.inputs.operand(T, K, g), pkg.inputs.operand(N, K, g)
+    dt, reps = cpu_time(lambda: oracle.gemm_torch(x.codes, w.codes, x.sf_blocked, w.sf_blocked, T, N, K), 3.0)
+    nbytes = (T + N) * K // 2 + (T + N) * K // 16 + 2 * T * N
+    return cpu_baseline(nbytes / dt / 1e9, "GB/s", f"the whole workload (T={T}, N={N}, K={K}), {reps} reps")
+
+
+def cpu_quant(pkg, rows=256, K=7168):
+    oracle = oracle_mod()
+    x = torch.randn((rows, K), generator=torch.Generator().manual_seed(0)).to(torch.float16).numpy()
+    dt, reps = cpu_time(lambda: oracle.quantize(x), 2.0)
+    nbytes = rows * K * 2 + rows * K // 2 + rows * K // 16
+    return cpu_baseline(nbytes / dt / 1e9, "GB/s", f"{rows} of 8192 rows x K={K} (numpy), {reps} reps")
+
+
+def headline_config(world):
+    """The `config` of the headline line, identical in both arms."""
+    return {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1" +
+            (f", row-sharded x{world}, all-gather fused into the kernel (NVLink peer stores)" if world > 1 else ""),
+            "M": HEADLINE["M"], "K": HEADLINE["K"], "L": HEADLINE["L"],
+            "l2": "flushed before every step (512 MiB write, then 256 MiB read)" +
+            ("; ranks aligned by a 1-element all-reduce before each step, outside the timed events"
+             if world > 1 else ""),
+            "parallelism": f"rows/{world}" if world > 1 else "single GPU"}
+
+
 def our_arm(args, world, rank, local):
     import __graft_entry__
     pkg = __graft_entry__.load_package()
@@ -403,9 +555,36 @@ def our_arm(args, world, rank, local):
         dist.all_gather_into_tensor(sh.gathered.view(-1), sh.local.view(-1))
         ev_mark(ev)
 
-    # correctness gate before timing (rank-local rows against a CPU row sample)
-    sh(pkg.custom_kernel, a, b, sfa, sfb)
-    torch.cuda.synchronize()
+    # correctness gate before timing
+    if world > 1:
+        # every rank: the fused all-gather's full output against the single-GPU
+        # kernel on the whole problem, bit for bit
+        a_full, sfa_full = to_dev(full.a), to_dev(full.sfa)
+        c_full = torch.empty((L, 1, M), dtype=torch.float16, device=dev).permute(2, 1, 0)
+        pkg.custom_kernel(a_full, b, sfa_full, sfb, c_full)
+        got = fused(a, b, sfa, sfb)
+        torch.cuda.synchronize()
+        ok = torch.equal(got, c_full) and pkg._lib.device_errors() == 0
+        max_diff = float((got.float() - c_full.float()).abs().max())
+        parity = {"status": "ok" if ok else "MISMATCH", "against": "single-GPU kernel, full problem, bit for bit",
+                  "max_abs_diff": max_diff}
+        del a_full, sfa_full
+    else:
+        # the CPU oracle on a row sample (north-star tolerance rtol = atol = 1e-2)
+        pkg.custom_kernel(a, b, sfa, sfb, c_local)
+        torch.cuda.synchronize()
+        oracle = oracle_mod()
+        rows = 512
+        ref = oracle.gemv_torch(full.a[:rows], full.b, full.sfa[:rows], full.sfb, rows, K, L).float()
+        got = c_local[:rows].float().cpu()
+        ok = bool(torch.allclose(got, ref, rtol=1e-2, atol=1e-2)) and pkg._lib.device_errors() == 0
+        max_diff = float((got - ref).abs().max())
+        parity = {"status": "ok" if ok else "MISMATCH", "against": f"CPU oracle, first {rows} rows, rtol=atol=1e-2",
+                  "max_abs_diff": max_diff}
+    if not all_ok(world, ok):
+        if rank == 0:
+            print(json.dumps({"error": "correctness gate failed", "parity": parity}), flush=True)
+        raise SystemExit(1)
 
     barrier(world)
     with ClockSampler(local) as clk:
@@ -421,6 +600,13 @@ def our_arm(args, world, rank, local):
         nccl_step, nccl_kern = max_over_ranks(world, [statistics.mean(sum(s) for s in nsegs),
                                                       statistics.mean(s[0] for s in nsegs)])
         mean_kern = nccl_kern
+        stamps = gather_stamps(fused, step_split, world)
+        grouped_ok, grouped_line = run_grouped_sharded_extra(pkg, flush, max(10, args.steps // 2), args.warmup,
+                                                             world, align, fp4_peak_tflops(pkg))
+        if not all_ok(world, grouped_ok):
+            if rank == 0:
+                print(json.dumps({"error": "grouped GEMM sharding gate failed", "grouped": grouped_line}), flush=True)
+            raise SystemExit(1)
     else:
         mean_kern = mean_step
     nbytes = full.nbytes_algorithmic()
@@ -454,6 +640,9 @@ def our_arm(args, world, rank, local):
         return None
     ncu_traffic = profiled_traffic("gemv_m16384_k16384_l1")
     kern_bytes = nbytes if world == 1 else nbytes * (hi - lo) / M
+    if ncu_traffic is not None and world > 1:
+        # the capture is of the 1-GPU launch; a rank streams its share of the rows
+        ncu_traffic = int(ncu_traffic * (hi - lo) / M)
     achieved = kern_bytes / (mean_kern * 1e-3) / 1e9
     line = {
         "metric": "NVFP4 GEMV HBM GB/s (M=K=16384, L=1)",
@@ -462,13 +651,8 @@ def our_arm(args, world, rank, local):
         "us_per_step_median": round(median_step * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e2m1/e4m3 in, f32 acc, f16 out",
         "data": "synthetic (seed 0; codes uniform 0..255, scales 2^u, u in [-3,3])",
-        "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1" +
-                   (f", row-sharded x{world}, all-gather fused into the kernel (NVLink peer stores)"
-                    if world > 1 else ""),
-                   "M": M, "K": K, "L": L, "l2": "flushed before every step (512 MiB write, then 256 MiB read)" +
-                   ("; ranks aligned by a 1-element all-reduce before each step, outside the timed events"
-                    if world > 1 else ""),
-                   "parallelism": f"rows/{world}" if world > 1 else "single GPU"},
+        "config": headline_config(world),
+        "parity": parity,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "peak_source": pk_kind,
                      "kernel_us": round(mean_kern * 1e3, 3), "algorithmic_bytes_per_launch": int(kern_bytes),
@@ -480,10 +664,13 @@ def our_arm(args, world, rank, local):
         "allgather": (None if world == 1 else {
             "fused_peer_store_us_per_step": round(mean_step * 1e3, 3),
             "nccl_us_per_step": round(nccl_step * 1e3, 3),
-            "kernel_only_us": round(mean_kern * 1e3, 3)}),
+            "kernel_only_us": round(mean_kern * 1e3, 3),
+            "fused_stamps_per_rank": stamps}),
         "clocks": clk.summary(),
         "wall_s_timed_region": round(t_wall, 3),
     }
+    if world > 1:
+        line["extras"] = [grouped_line]
     if world == 1:
         gbs, sample, threads = cpu_gemv_sample(pkg, M, K, L, target_s=args.cpu_seconds)
         line["cpu_baseline"] = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -494,6 +681,9 @@ def our_arm(args, world, rank, local):
                               run_gemv_b2b_extra(pkg, M, K, L)]
             for e in line["extras"]:
                 e["hbm_frac"] = round(e["gbs"] / pk["hbm_gbs"], 4)
+            for e, (m, k, l) in zip(line["extras"][:2], ((256, 1024, 1), (4096, 14336, 8))):
+                g, smp, _ = cpu_gemv_sample(pkg, m, k, l, target_s=2.0, max_rows=512)
+                e["cpu_baseline"] = cpu_baseline(g, "GB/s", smp)
             peak_tf = fp4_peak_tflops(pkg)
             line["fp4_peak_tflops_measured"] = round(peak_tf, 1)
             line["fp4_peak_tflops_gemm_pattern"] = round(fp4_peak_tflops(pkg, pattern=1), 1)
@@ -501,6 +691,8 @@ def our_arm(args, world, rank, local):
                                run_grouped_extra(pkg, flush, 20, 3, peak_tf, pk["hbm_gbs"]),
                                run_skinny_extra(pkg, flush, 30, 3, pk["hbm_gbs"]),
                                run_quant_extra(pkg, flush, 30, 3, pk["hbm_gbs"])]
+            for e, fn in zip(line["extras"][-4:], (cpu_dual, cpu_grouped, cpu_skinny, cpu_quant)):
+                e["cpu_baseline"] = fn(pkg)
             line["gpu_launches_extras_note"] = "extras are separate timed loops, not part of gpu_launches"
     return line
 
@@ -536,7 +728,7 @@ def reference_arm(args, world, rank, local):
         "ms_per_step": round(full_bytes / (gbs * 1e9) * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "e2m1/e4m3 in, f32 acc, f16 out",
         "data": "synthetic (seed 0)",
-        "config": {"workload": "config 1: NVFP4 GEMV M=16384 K=16384 L=1", "M": M, "K": K, "L": L},
+        "config": headline_config(world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"{rows} of {M} rows per step (fp32 dequantise + matmul, torch CPU)",
                          "host_cpus": os.cpu_count()},
@@ -580,6 +772,7 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup()
+    torch.set_num_threads(os.cpu_count() or 1)   # torchrun sets OMP_NUM_THREADS=1; the CPU legs use every core
     if args.profile:
         import __graft_entry__
         pkg = __graft_entry__.load_package()

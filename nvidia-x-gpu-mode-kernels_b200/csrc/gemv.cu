@@ -518,9 +518,12 @@ int launch_generic(const GemvArgs& p, cudaStream_t stream) {
   return check_launch("gemv_generic_kernel");
 }
 
-// Configuration by shape: the row slice per stage matches K (one 2 KB box row
-// when K allows), and small problems use short tiles so that every SM gets
-// work.
+// Configuration by shape.  The stage width KTB (bytes of a row per stage) is
+// chosen from K alone: a row's f32 summation order, and so every bit of its
+// result, depends on KTB and on nothing else (not on the row tile, the warp
+// count, the grid, M, L or the rank's share), so a row-sharded GEMV returns
+// exactly the single-GPU bits.  Small problems then use short tiles and more
+// CTAs per SM so that every SM gets work.
 // With grid_out set, only reports the grid the launch would use.
 int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullptr) {
   const int64_t kb = p.K / 2;
@@ -530,24 +533,21 @@ int gemv_dispatch(const GemvArgs& p, cudaStream_t st, int64_t* grid_out = nullpt
   // bytes is 3.5 slices of 2 KB (a half-empty last stage per tile, 52.3 us on
   // config 2) but exactly 7 slices of 1 KB (48.6 us)
   auto pad = [kb](int64_t w) { return ((kb + w - 1) / w) * w - kb; };
-  const bool wide = kb >= 2048 && pad(2048) <= pad(1024);
-  if (rows < sms * 16) {
-    // fewer than 16 rows per SM (the per-rank share of a row-sharded GEMV at
-    // 8 GPUs): 4-row tiles, four CTAs per SM (M=2048, K=16384: 11.5 vs 12.0 us
-    // with 2 KB stages; the fused all-gather keeps the 1 KB-stage form it was
-    // measured with at 8 ranks)
-    if (kb <= 512) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
-    if (wide && p.world == 0) return launch_tma<GemvCfg<4, 2048, 4, 4, 4>>(p, st, grid_out);
-    return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
+  const int ktb = (kb >= 2048 && pad(2048) <= pad(1024)) ? 2048 : (kb >= 1024 ? 1024 : 512);
+  if (ktb == 2048) {
+    // fewer than 16 rows per SM (the 8-rank share of config 1): 4-row tiles,
+    // four CTAs per SM (M=2048, K=16384: 11.5 vs 12.0 us with 1 KB stages)
+    if (rows < sms * 16) return launch_tma<GemvCfg<4, 2048, 4, 4, 4>>(p, st, grid_out);
+    // fewer than two 16-row tiles per SM (the 4-rank share): 8-row tiles,
+    // two CTAs per SM
+    if (rows < sms * 32) return launch_tma<GemvCfg<8, 2048, 4, 4, 2>>(p, st, grid_out);
+    return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
   }
-  // fewer than two 16-row tiles per SM: two CTAs per SM spread them over
-  // twice the CTAs (M=4096, K=16384: 14.9 vs 16.1 us).  Not with the fused
-  // all-gather, whose completion costs a system fence and a count per CTA:
-  // there the 296-CTA grid made the 4-rank step slower (35.2 vs 34.0 us for
-  // kernel + NCCL).
-  if (rows < sms * 32 && kb >= 1024 && p.world == 0) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
-  if (wide) return launch_tma<GemvCfg<16, 2048, 4, 8, 1>>(p, st, grid_out);
-  if (kb >= 1024) return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
+  if (ktb == 1024) {
+    if (rows < sms * 16) return launch_tma<GemvCfg<4, 1024, 3, 4, 4>>(p, st, grid_out);
+    return launch_tma<GemvCfg<16, 1024, 4, 8, 2>>(p, st, grid_out);
+  }
+  if (rows < sms * 16) return launch_tma<GemvCfg<2, 512, 2, 2, 8>>(p, st, grid_out);
   return launch_tma<GemvCfg<16, 512, 4, 8, 2>>(p, st, grid_out);
 }
 

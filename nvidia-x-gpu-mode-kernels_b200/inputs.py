@@ -76,9 +76,21 @@ class Operand:
 GEMM_SCALE_EXP = (-5, -3)
 
 
-def operand(rows: int, K: int, g: torch.Generator, device="cpu", scale_exp=GEMM_SCALE_EXP) -> Operand:
-    codes = _codes(g, (rows, K // 2))
-    sf = _scales(g, (rows, K // 16), *scale_exp)
+def operand(rows: int, K: int, g: torch.Generator, device="cpu", scale_exp=GEMM_SCALE_EXP,
+            all_scale_bytes: bool = False, code_mask: int = 0xFF, keep: float = 1.0) -> Operand:
+    """Seeded operand.  Scales are 2^u, u uniform in ``scale_exp``, or, with
+    ``all_scale_bytes``, uniform over every positive finite e4m3 byte
+    0x01..0x7E (subnormals and mantissa bits included).  ``code_mask`` ANDs
+    every code byte (0x99 keeps the values 0 and +-0.5, which keeps products of
+    large scales inside fp16) and ``keep`` zeroes each code byte with
+    probability 1 - keep."""
+    codes = _codes(g, (rows, K // 2)) & code_mask
+    if keep < 1.0:
+        codes = torch.where(torch.rand((rows, K // 2), generator=g) < keep, codes, torch.zeros_like(codes))
+    if all_scale_bytes:
+        sf = torch.randint(1, 127, (rows, K // 16), dtype=torch.uint8, generator=g)
+    else:
+        sf = _scales(g, (rows, K // 16), *scale_exp)
     return Operand(codes.to(device), to_blocked(sf).to(device), rows, K)
 
 

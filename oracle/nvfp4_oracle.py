@@ -221,6 +221,32 @@ def grouped_gemm(groups, acc=np.float32):
     return outs
 
 
+def dequant_matrix_torch(codes, sf_blocked, rows: int, K: int) -> torch.Tensor:
+    """torch CPU form of ``dequant_matrix`` (multi-threaded; the timed CPU
+    baseline of the GEMMs): codes [rows, K/2] bytes + blocked scales ->
+    [rows, K] fp32, via the same 16- and 256-entry decode tables."""
+    lut2 = torch.from_numpy(E2M1_LUT)
+    lut8 = torch.from_numpy(E4M3_LUT)
+    c = codes if codes.dtype == torch.uint8 else codes.view(torch.uint8)
+    c = c[:rows, : K // 2].long()
+    v = torch.stack((lut2[c & 15], lut2[c >> 4]), dim=-1).reshape(rows, K)
+    s = torch.from_numpy(from_blocked_ref(sf_blocked, rows, K // 16).astype(np.int64))
+    return (v.view(rows, K // 16, 16) * lut8[s][:, :, None]).view(rows, K)
+
+
+def gemm_torch(a, b, sfa_blocked, sfb_blocked, M: int, N: int, K: int) -> torch.Tensor:
+    """``gemm`` with torch CPU ops: fp32 C[M, N] (no reference code exists)."""
+    return dequant_matrix_torch(a, sfa_blocked, M, K) @ dequant_matrix_torch(b, sfb_blocked, N, K).T
+
+
+def dual_gemm_torch(x, w1, w2, sfx, sfw1, sfw2, M: int, N: int, K: int) -> torch.Tensor:
+    """``dual_gemm`` with torch CPU ops: fp16 silu(X W1^T) * (X W2^T)."""
+    X = dequant_matrix_torch(x, sfx, M, K)
+    g = X @ dequant_matrix_torch(w1, sfw1, N, K).T
+    u = X @ dequant_matrix_torch(w2, sfw2, N, K).T
+    return (torch.nn.functional.silu(g) * u).to(torch.float16)
+
+
 # ---------------------------------------------------------------------------
 # Quantiser (north-star "next" row: fp16 activations -> NVFP4).  No reference
 # code exists; these are the rounding rules the library documents.

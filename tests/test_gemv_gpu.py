@@ -178,3 +178,23 @@ def test_gemv_forward_matches_custom_kernel(pkg, oracle, cuda):
     assert torch.equal(c[:200, :, :1], want[:200, :, :1])
     assert torch.isnan(c[200:]).all() and torch.isnan(c[:, :, 1:]).all()
     assert pkg._lib.device_errors() == 0
+
+
+@pytest.mark.parametrize("M,K,L", [(16384, 16384, 1), (4096, 14336, 8), (1000, 2048, 3)])
+def test_row_shares_are_bit_identical_to_single_gpu(pkg, cuda, M, K, L):
+    """What a rank of an N-way row-sharded GEMV computes (its rows alone, with
+    the launch shape chosen for that share) equals the single-GPU rows bit for
+    bit, for N = 2, 4, 8: the stage width, which alone fixes the summation
+    order, depends on K only."""
+    x = pkg.inputs.gemv_inputs(M, K, L, seed=1, device=cuda)
+    pkg.custom_kernel(*x.as_tuple())
+    torch.cuda.synchronize()
+    full = x.c.clone()
+    for world in (2, 4, 8):
+        for rank in range(world):
+            lo, hi = pkg.sharded.row_split(M, world, rank)
+            sub = lambda t: t[lo:hi].permute(2, 0, 1).contiguous().permute(1, 2, 0)
+            c = torch.empty((L, 1, hi - lo), dtype=torch.float16, device=cuda).permute(2, 1, 0)
+            pkg.custom_kernel(sub(x.a), x.b, sub(x.sfa), x.sfb, c)
+            torch.cuda.synchronize()
+            assert torch.equal(c.view(torch.int16), full[lo:hi].view(torch.int16)), (world, rank)

@@ -87,3 +87,51 @@ def test_gloo_world2_gather():
     for p in procs:
         p.join(timeout=30)
     assert sorted(res) == [(0, True, True), (1, True, True)]
+
+
+def _failing_worker(rank, world, port, q):
+    """Rank 1 leaves before the output all-gather (between steps, nothing in
+    flight); rank 0 must see its gather fail within the process group's
+    timeout instead of waiting forever."""
+    import sys
+    import time
+    from datetime import timedelta
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import __graft_entry__
+    pkg = __graft_entry__.load_package()
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    Ms, N = [5, 3, 7], 4
+    gs = pkg.sharded.ShardedGroupedGemm(Ms, N, 64, device=torch.device("cpu"))
+    fake = lambda al, bl, sal, sbl, cl: [c.fill_(1.0) for c in cl]
+    gs(fake, [None] * len(gs.mine), None, None, None)      # one healthy step on both ranks
+    if rank == 1:
+        q.put((rank, "left", 0.0))
+        q.close()
+        q.join_thread()                                      # flush the message before leaving
+        os._exit(0)                                          # leaves without joining step 2
+    t0 = time.monotonic()
+    try:
+        gs(fake, [None] * len(gs.mine), None, None, None)
+        q.put((rank, "completed", time.monotonic() - t0))
+    except Exception as e:  # gloo reports the lost peer or the timeout
+        q.put((rank, "raised " + type(e).__name__, time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.timeout(120)
+def test_gloo_rank_failure_is_detected():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=30)
+    assert res[1][1] == "left"
+    assert res[0][1].startswith("raised"), res
+    assert res[0][2] < 30.0, res    # well inside the test's own limit: the 5 s group timeout or an earlier reset
