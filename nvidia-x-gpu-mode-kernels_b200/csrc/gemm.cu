@@ -40,6 +40,7 @@
 
 #include "gemm_cfg.cuh"
 #include "gemm_kernel.cuh"
+#include "gemm_pair.cuh"
 
 namespace nvfp4 {
 
@@ -60,6 +61,50 @@ int launch_gemm(const GemmParams<MAXG>& P, cudaStream_t stream) {
   if (grid < 1) return NVFP4_OK;
   gemm_kernel<C, MAXG><<<grid, C::THREADS, C::SMEM, stream>>>(P);
   return check_launch("gemm_kernel");
+}
+
+template <class C, int MAXG>
+int launch_pair(const GemmParams<MAXG>& P, cudaStream_t stream) {
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return fail(NVFP4_ERR_UNSUPPORTED, "device index out of range");
+  auto kern = pair_kernel<C, MAXG>;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(pair gemm)");
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n < 1) return fail(NVFP4_ERR_UNSUPPORTED, "no CTA pairs fit on this device");
+    max_pairs[dev] = n;
+    attr_set[dev] = true;
+  }
+  int pairs = max_pairs[dev];
+  if (P.total_tiles < pairs) pairs = P.total_tiles;
+  if (pairs < 1) return NVFP4_OK;
+  cfg.gridDim = dim3(2 * pairs);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, P);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(pair gemm)");
+  return check_launch("pair_kernel");
+}
+
+template <class C, int MAXG>
+int launch_any(const GemmParams<MAXG>& P, cudaStream_t stream) {
+  if constexpr (C::PAIR) return launch_pair<C, MAXG>(P, stream);
+  else return launch_gemm<C, MAXG>(P, stream);
 }
 
 int operand_map(CUtensorMap* m, const void* p, int64_t rows, int64_t K, int64_t ld, int box_rows) {
@@ -115,8 +160,8 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   GemmParams<1> P;
   std::memset(&P, 0, sizeof(P));
   GemmGroup& G = P.g[0];
-  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::BN)) ||
-      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::BN)))
+  if ((rc = operand_map(&G.ta, a, M, K, lda, BM)) || (rc = operand_map(&G.tb, b1, N, K, ldb, C::B_BOX)) ||
+      (rc = operand_map(&G.tb2, b2, N, K, ldb, C::B_BOX)))
     return rc;
   if ((rc = sf_map(&G.tsa, sfa, M, K, 1, C::KPS)) || (rc = sf_map(&G.tsb, sfb1, N, K, C::NB, C::KPS)) ||
       (rc = sf_map(&G.tsb2, sfb2, N, K, C::NB, C::KPS)))
@@ -125,14 +170,14 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
   G.ldc = ldc;
   G.vec_ok = vec_ok(c, ldc);
   G.M = (int)M; G.N = (int)N; G.K = (int)K;
-  G.tiles_m = (int)((M + BM - 1) / BM);
+  G.tiles_m = (int)((M + C::TILE_M - 1) / C::TILE_M);
   G.tiles_n = (int)((N + C::BN - 1) / C::BN);
   G.tile_begin = 0;
   P.ngroups = 1;
   P.total_tiles = G.tiles_m * G.tiles_n;
   P.err = device_error_word();
   if (!P.err) return fail(NVFP4_ERR_CUDA, "nvfp4_dual_gemm: cannot resolve the device error word");
-  return launch_gemm<C, 1>(P, static_cast<cudaStream_t>(stream));
+  return launch_any<C, 1>(P, static_cast<cudaStream_t>(stream));
 }
 
 }  // namespace nvfp4
@@ -140,10 +185,12 @@ int dual_run(const void* a, const void* b1, const void* b2, const void* sfa, con
 extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa, const void* sfb1,
                                const void* sfb2, void* c, int64_t M, int64_t N, int64_t K, int64_t lda,
                                int64_t ldb, int64_t ldc, void* stream) {
-  // two 512-element K stages of 108 KB: half the stage handshakes of four 256-element
-  // stages at the same bytes in flight (30.9 vs 33.3 us on the dual workload, same box)
-  return dual_run<GemmCfg<128, true, 2, 0, 2>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb,
-                                                                   ldc, stream);
+  // CTA pairs (256 x 128 tiles per B operand, 5 stages of 38 KB) when K is a
+  // multiple of the 256-element stage: 16.x vs 30.6 us on the dual workload.
+  // Otherwise the single-CTA kernel with two 512-element K stages of 108 KB.
+  if (K % 256 == 0)
+    return dual_run<PairCfg<128, 5, true>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb, ldc, stream);
+  return dual_run<GemmCfg<128, true, 2, 0, 2>>(a, b1, b2, sfa, sfb1, sfb2, c, M, N, K, lda, ldb, ldc, stream);
 }
 
 namespace nvfp4 {
@@ -201,7 +248,7 @@ int grouped_launches(const nvfp4_group* groups, int num_groups, void* stream) {
           (rc = check_operand("b", q.b, q.sfb, q.N, q.K, q.ldb)) || (rc = check_out(q.c, q.N, q.ldc)))
         return rc;
       GemmGroup& G = P.g[n];
-      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::BN)))
+      if ((rc = operand_map(&G.ta, q.a, q.M, q.K, q.lda, BM)) || (rc = operand_map(&G.tb, q.b, q.N, q.K, q.ldb, C::B_BOX)))
         return rc;
       if ((rc = sf_map(&G.tsa, q.sfa, q.M, q.K, 1, C::KPS)) || (rc = sf_map(&G.tsb, q.sfb, q.N, q.K, C::NB, C::KPS)))
         return rc;
@@ -209,7 +256,7 @@ int grouped_launches(const nvfp4_group* groups, int num_groups, void* stream) {
       G.ldc = q.ldc;
       G.vec_ok = vec_ok(q.c, q.ldc);
       G.M = (int)q.M; G.N = (int)q.N; G.K = (int)q.K;
-      G.tiles_m = (int)((q.M + BM - 1) / BM);
+      G.tiles_m = (int)((q.M + C::TILE_M - 1) / C::TILE_M);
       G.tiles_n = (int)((q.N + C::BN - 1) / C::BN);
       G.tile_begin = tiles;
       tiles += G.tiles_m * G.tiles_n;
@@ -220,7 +267,7 @@ int grouped_launches(const nvfp4_group* groups, int num_groups, void* stream) {
     P.ngroups = n;
     P.total_tiles = tiles;
     P.err = err;
-    int rc = launch_gemm<C, MAXG>(P, static_cast<cudaStream_t>(stream));
+    int rc = launch_any<C, MAXG>(P, static_cast<cudaStream_t>(stream));
     if (rc) return rc;
   }
   return NVFP4_OK;
@@ -238,6 +285,11 @@ int grouped_run(const nvfp4_group* groups, int num_groups, void* stream) {
 }  // namespace nvfp4
 
 extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream) {
+  // CTA pairs (256 x 256 tiles, 5 stages) when every group's K is a multiple
+  // of the 256-element stage; the single-CTA kernel handles the rest
+  bool k256 = groups != nullptr && num_groups > 0;
+  for (int i = 0; k256 && i < num_groups; ++i) k256 = groups[i].M == 0 || groups[i].K % 256 == 0;
+  if (k256) return grouped_run<PairCfg<256, 5>>(groups, num_groups, stream);
   return grouped_run<GemmCfg<256, false, 4>>(groups, num_groups, stream);
 }
 

@@ -77,6 +77,9 @@ struct GemmCfg {
   // warp 0 producer, warp 1 MMA, warps 2-5 epilogue, warps 6-9 scale staging
   static constexpr int THREADS = 320;
   static constexpr uint32_t IDESC = tc::idesc_mxf4nvf4(BM, BN);
+  static constexpr bool PAIR = false;
+  static constexpr int TILE_M = BM;   // output rows per tile
+  static constexpr int B_BOX = BN;    // B rows per TMA box
 };
 
 __device__ __forceinline__ int find_group(const GemmGroup* g, int ng, int t) {
