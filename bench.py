@@ -412,15 +412,14 @@ def gather_rows(world, values):
 
 def gather_stamps(fused, step, world, n=20):
     """Per-rank medians over n synchronised calls of the fused gather's
-    %globaltimer stamps: own rows published and all ranks' rows present, in us
+    %globaltimer stamps: CTA 0's rows sent and all ranks' rows present, in us
     after the rank's launch began, plus each rank's start relative to the
     earliest (GPU timers of one node; offsets between them are not removed)."""
     pub, seen, starts = [], [], []
     for _ in range(n):
         step([])
         torch.cuda.synchronize()
-        w = fused.flags[32:38].cpu().numpy().view("uint32").astype("uint64")
-        t0, t1, t2 = (int(w[2 * i]) | (int(w[2 * i + 1]) << 32) for i in range(3))
+        t0, t1, t2 = fused.stamps()
         pub.append((t1 - t0) / 1e3)
         seen.append((t2 - t0) / 1e3)
         starts.append(float(t0))

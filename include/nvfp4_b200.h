@@ -79,34 +79,40 @@ NVFP4_API int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid);
 /*
  * Row-sharded GEMV with the output all-gather fused in (one launch per rank,
  * one rank per GPU).  This rank computes rows [m_off, m_off + M_local) of the
- * full output (its a / sfa hold only those rows) and stores each result row
- * into EVERY rank's full-size output buffer peer_out[r] (device pointers valid
- * on this GPU: peer memory over NVLink, e.g. from torch symmetric memory), with
- * element strides c_sm / c_sl.  peer_flags[r] is rank r's flag buffer: at least
- * 64 zero-initialised 32-bit words in memory every rank can reach.  Word 16 of
- * this rank's buffer counts its finished CTAs (the last one resets it to 0); the
- * last CTA writes `epoch` into word `rank` of every rank's buffer and waits until
- * this rank's words 0..world-1 all hold `epoch`, so the launch ends with every
- * rank's rows present locally.  Words 32-37 of this rank's buffer receive three
- * 64-bit %globaltimer stamps (low word first): the launch's start, the moment this
- * rank's rows were all published, and the moment every rank's rows had arrived.
- * `epoch` is the 1-based count of calls made with these flag buffers (the same
- * on every rank; the shape must stay the same between calls).  epoch == 0
- * selects device-epoch mode: the kernel keeps the count in word 20 of this
- * rank's flag buffer, so a captured CUDA graph of the call advances it on every
- * replay (use one mode per set of flag buffers).  The wait is
- * bounded (2 s by default, see nvfp4_set_peer_wait_ns; error bit 16 in
- * nvfp4_device_errors()).  Requires the aligned
- * (TMA) path; world <= 8.  Replaces "nvfp4_gemv_forward + an output
- * all-gather" (the reference has no distributed code; the north star asks for
- * row sharding with an output all-gather).
+ * full M_total-row output (its a / sfa hold only those rows) and sends each
+ * result to every rank; the launch returns once `out` holds the full output
+ * [M_total, 1, L] (fp16, element strides c_sm / c_sl, on this GPU).
+ *
+ * peer_stage[r] is rank r's staging buffer, a device pointer valid on this GPU
+ * (peer memory over NVLink, e.g. from torch symmetric memory), 8-byte aligned,
+ * zero-initialised, of at least 64 + 2 * M_total * L 32-bit words.  Protocol:
+ * element (m, l) travels as one 64-bit line (epoch << 32 | fp16 bits) to index
+ * 32 + l * M_total + m (in 64-bit units) of every rank's buffer; a naturally
+ * aligned 64-bit store is single-copy atomic, so a line carrying this call's
+ * epoch carries this call's value and no fence or counter gates it.  Each CTA
+ * then copies its slice of the lines into `out`, waiting for each to carry the
+ * epoch.  Words 0-63 of this rank's buffer are control words: 16 counts
+ * finished CTAs (reset by the last one), 20 holds the epoch in device-epoch
+ * mode, 32-37 receive three 64-bit %globaltimer stamps (low word first): the
+ * launch's start, CTA 0 having sent its rows, and the last CTA holding its
+ * slice.
+ *
+ * `epoch` is the 1-based count of calls made with these staging buffers (the
+ * same on every rank; the shape must stay the same between calls).
+ * epoch == 0 selects device-epoch mode: the kernel keeps the count in word 20
+ * of this rank's buffer, so a captured CUDA graph of the call advances it on
+ * every replay (use one mode per set of buffers).  Every wait is bounded (2 s
+ * by default, see nvfp4_set_peer_wait_ns; error bit 16 in nvfp4_device_errors()).
+ * Requires the aligned (TMA) path; world <= 8.  Replaces "nvfp4_gemv_forward
+ * + an output all-gather" (the reference has no distributed code; the north
+ * star asks for row sharding with an output all-gather).
  */
 NVFP4_API int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
                                    int64_t M_local, int64_t K, int64_t L,
                                    int64_t a_sm, int64_t a_sl, int64_t b_sl,
                                    int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
-                                   void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
-                                   uint32_t* const* peer_flags, int world, int rank, uint32_t epoch,
+                                   void* out, int64_t c_sm, int64_t c_sl, int64_t m_off, int64_t M_total,
+                                   void* const* peer_stage, int world, int rank, uint32_t epoch,
                                    void* stream);
 
 /*

@@ -42,7 +42,7 @@ SIGNATURES: dict[str, list] = {
     "nvfp4_gemv_grid": [I64, I64, I64, ctypes.POINTER(I64)],
     "nvfp4_set_peer_wait_ns": [ctypes.c_uint64],
     "nvfp4_gemv_allgather": [VP, VP, VP, VP, I64, I64, I64, I64, I64, I64, I64, I64, I64,
-                             ctypes.POINTER(VP), I64, I64, I64, ctypes.POINTER(VP), ctypes.c_int, ctypes.c_int,
+                             VP, I64, I64, I64, I64, ctypes.POINTER(VP), ctypes.c_int, ctypes.c_int,
                              ctypes.c_uint32, VP],
 }
 

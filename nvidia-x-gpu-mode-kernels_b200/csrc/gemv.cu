@@ -44,9 +44,12 @@ namespace nvfp4 {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kCtaCounter = 16;   // flag-buffer word counting this rank's finished CTAs (reset per call)
-constexpr int kEpochWord = 20;    // flag-buffer word holding the last epoch (device-epoch mode)
-constexpr int kStampWord = 32;    // words 32-37: %globaltimer at start / rows published / all peers seen
+// Staging buffer of the fused all-gather (32-bit words): control words first,
+// then one 64-bit line per output element from word kLineWord on.
+constexpr int kCtaCounter = 16;   // counts this rank's finished CTAs (reset per call)
+constexpr int kEpochWord = 20;    // the last epoch (device-epoch mode)
+constexpr int kStampWord = 32;    // words 32-37: %globaltimer at start / rows sent / all rows present
+constexpr int kLineWord = 64;     // first line: element e at 64-bit index kLineWord / 2 + e
 
 
 struct GemvArgs {
@@ -58,15 +61,17 @@ struct GemvArgs {
   int64_t M, K, L;
   int64_t a_sm, a_sl, b_sl, sfa_sm, sfa_sl, sfb_sl, c_sm, c_sl;
   uint32_t* err;
-  // Fused all-gather (world > 0): rows also go to every rank's output at row
-  // offset m_off, then every CTA adds one arrival to every rank's flag.
-  __half* peer_c[kMaxRanks];
-  uint32_t* peer_flag[kMaxRanks];
+  // Fused all-gather (world > 0): every result also goes, as one 64-bit line
+  // (epoch << 32 | fp16 bits), to element index l * M_total + m_off + row of
+  // every rank's staging buffer; then each CTA unpacks its slice of the full
+  // output from this rank's staging buffer into c, once the slice's lines
+  // carry this call's epoch.
+  uint64_t* peer_stage[kMaxRanks];
   int world;
   int rank;
   int64_t m_off;
-  uint32_t epoch;    // 1-based call count of this gather (same on every rank)
-  int vec_rows;      // c_sm == 1 and 16-byte aligned row runs: whole-piece peer stores
+  int64_t M_total;
+  uint32_t epoch;    // 1-based call count of this gather (same on every rank); 0 = device epoch
   uint64_t peer_wait_ns;   // budget of the wait for the other ranks' rows
 };
 
@@ -93,8 +98,7 @@ struct GemvCfg {
   static constexpr int STAGE_BYTES = ((OFF_SFB + SFK) + 127) / 128 * 128;
   static constexpr uint32_t TX = ROWS * KTB + ROWS * SFK + KTB + SFK;
   static constexpr int OFF_RED = STAGES * STAGE_BYTES;                  // float [2][ROWS][NCH]
-  static constexpr int OFF_HB = OFF_RED + 2 * ROWS * NCH * 4;          // __half [2][ROWS] (fused gather)
-  static constexpr int OFF_BAR = (OFF_HB + 2 * ROWS * 2 + 15) / 16 * 16;
+  static constexpr int OFF_BAR = (OFF_RED + 2 * ROWS * NCH * 4 + 15) / 16 * 16;
   static constexpr int SMEM = OFF_BAR + 2 * STAGES * 8 + 128;           // + alignment slack
   static_assert(KTB % 512 == 0 && KTB <= 2048, "KTB: 512-byte chunks, box row <= 256 u64");
   static_assert(CW % NCH == 0 && ROWS % GROUPS == 0, "warps must tile (rows x chunks)");
@@ -164,15 +168,22 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
   // the previous kernel on the stream; wait for it before touching global
   // memory (a no-op when launched without the attribute).
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  uint32_t epoch_at_start = 0;
-  if (p.world > 0 && p.epoch == 0 && threadIdx.x == 0)
-    epoch_at_start = *reinterpret_cast<volatile uint32_t*>(p.peer_flag[p.rank] + kEpochWord) + 1u;
-
-  if (p.world > 0 && blockIdx.x == 0 && threadIdx.x == 0) {
-    const uint64_t t = globaltimer();
-    p.peer_flag[p.rank][kStampWord] = (uint32_t)t;
-    p.peer_flag[p.rank][kStampWord + 1] = (uint32_t)(t >> 32);
+  // fused all-gather: this launch's epoch, for every thread.  Device-epoch
+  // mode (p.epoch == 0) numbers the launch (stored + 1); every CTA reads the
+  // word before the last CTA (which counts in after all others have started)
+  // stores the new value.
+  __shared__ uint32_t s_epoch;
+  uint32_t* const ctl = p.world > 0 ? reinterpret_cast<uint32_t*>(p.peer_stage[p.rank]) : nullptr;
+  if (p.world > 0 && threadIdx.x == 0) {
+    s_epoch = p.epoch ? p.epoch : *reinterpret_cast<volatile uint32_t*>(ctl + kEpochWord) + 1u;
+    if (blockIdx.x == 0) {
+      const uint64_t t = globaltimer();
+      ctl[kStampWord] = (uint32_t)t;
+      ctl[kStampWord + 1] = (uint32_t)(t >> 32);
+    }
   }
+  __syncthreads();
+  const uint32_t epoch = s_epoch;
   const int64_t M = p.M;
   const int nk = (int)((p.K / 2 + C::KTB - 1) / C::KTB);
   const int64_t tpl = (M + C::ROWS - 1) / C::ROWS;  // tiles per batch
@@ -261,84 +272,77 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
       if (lane == 0) rb[(group * C::RPW + j) * C::NCH + chunk] = v;
     }
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
-    // fused gather with contiguous output rows: stage the tile's results and
-    // send each peer whole 16-byte pieces instead of one 2-byte store per row
-    const bool vec = (C::ROWS % 8 == 0) && p.world > 0 && p.vec_rows && m0 + C::ROWS <= M;
-    __half* hb = reinterpret_cast<__half*>(smem + C::OFF_HB) + parity * C::ROWS;
-    for (int row = threadIdx.x; row < C::ROWS; row += C::CW * 32) {
-      float v = 0.f;
+    if (p.world == 0) {
+      for (int row = threadIdx.x; row < C::ROWS; row += C::CW * 32) {
+        float v = 0.f;
 #pragma unroll
-      for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
-      if (vec) {
-        hb[row] = __float2half_rn(v);
-      } else if (m0 + row < M) {
-        const __half hv = __float2half_rn(v);
-        if (p.world == 0) {
-          p.c[l * p.c_sl + (m0 + row) * p.c_sm] = hv;
-        } else {
-          const int64_t off = l * p.c_sl + (p.m_off + m0 + row) * p.c_sm;
-          for (int r = 0; r < p.world; ++r) p.peer_c[r][off] = hv;   // NVLink peer stores
-        }
+        for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
+        if (m0 + row < M) p.c[l * p.c_sl + (m0 + row) * p.c_sm] = __float2half_rn(v);
       }
-    }
-    if (vec) {
-      asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
-      constexpr int PIECES = C::ROWS / 8 > 0 ? C::ROWS / 8 : 1;
-      const int t = threadIdx.x;
-      if (t < p.world * PIECES) {
-        const int r = t / PIECES, q = t % PIECES;
-        const uint4 v = *reinterpret_cast<const uint4*>(hb + 8 * q);
-        *reinterpret_cast<uint4*>(p.peer_c[r] + l * p.c_sl + p.m_off + m0 + 8 * q) = v;   // NVLink peer store
+    } else {
+      // one 64-bit line per (row, rank): thread t sends row t % ROWS to rank
+      // t / ROWS.  A naturally aligned 64-bit store is single-copy atomic, so a
+      // line that carries this call's epoch carries this call's value: no
+      // fence or count is needed before the receiver may use it.
+      for (int t = threadIdx.x; t < C::ROWS * p.world; t += C::CW * 32) {
+        const int row = t % C::ROWS, r = t / C::ROWS;
+        if (m0 + row >= M) continue;
+        float v = 0.f;
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
+        const uint64_t line = ((uint64_t)epoch << 32) | __half_as_ushort(__float2half_rn(v));
+        uint64_t* dst = p.peer_stage[r] + kLineWord / 2 + l * p.M_total + p.m_off + m0 + row;
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(dst), "l"(line) : "memory");   // NVLink peer store
       }
     }
   }
   if (p.world > 0) {
-    // Completion, two levels.  Each CTA counts itself into this rank's local
-    // counter (word kCtaCounter of its flag buffer); the CTA that completes the
-    // count is last on this GPU, so every row of this rank has been stored: it
-    // resets the counter for the next call, publishes the rows (system fence)
-    // and writes the call's epoch into word `rank` of every rank's flag buffer,
-    // then waits until every rank's word holds this epoch, i.e. all rows of all
-    // ranks have landed here.  Words kStampWord.. record when each step happened.
+    // Completion: CTA b unpacks slice b of the full output (all ranks' rows)
+    // from this rank's staging buffer, waiting (bounded) for each line to carry
+    // this call's epoch; the launch ends when every slice is in c.  Thread 0 of
+    // the CTA that finishes last resets the CTA count, stamps the time and, in
+    // device-epoch mode, stores the epoch for the next launch.
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
-    if (threadIdx.x == 0) {
-      // epoch 0 = device-epoch mode: this launch is number (stored + 1).  Every
-      // CTA reads the word before the last CTA (which counts in after all the
-      // others have started) stores the new value.
-      const uint32_t epoch = p.epoch ? p.epoch : epoch_at_start;
-      // this CTA's stores went to other GPUs too: order them at system scope
-      // before it counts itself in, so the last CTA's release covers them
-      __threadfence_system();
-      uint32_t* mine = p.peer_flag[p.rank];
-      const uint32_t done = atomicAdd(mine + kCtaCounter, 1u) + 1u;
-      if (done == gridDim.x) {
-        mine[kCtaCounter] = 0u;   // every CTA of this launch has counted in
-        __threadfence_system();
-        const uint64_t ts = globaltimer();
-        mine[kStampWord + 2] = (uint32_t)ts;
-        mine[kStampWord + 3] = (uint32_t)(ts >> 32);
-        for (int r = 0; r < p.world; ++r)
-          // relaxed: the system fence above already orders every row store
-          // before these; a release per store would fence (and wait) per peer
-          asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p.peer_flag[r] + p.rank), "r"(epoch)
-                       : "memory");
-        const uint64_t t0 = globaltimer();
-        for (int r = 0; r < p.world; ++r) {
-          for (uint32_t it = 0;; ++it) {
-            uint32_t v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine + r) : "memory");
-            if ((int32_t)(v - epoch) >= 0) break;
-            if ((it & 63u) == 63u && globaltimer() - t0 > p.peer_wait_ns) {
-              atomicOr(p.err, kDevErrTimeoutPeer);
-              break;
-            }
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      const uint64_t ts = globaltimer();
+      ctl[kStampWord + 2] = (uint32_t)ts;
+      ctl[kStampWord + 3] = (uint32_t)(ts >> 32);
+    }
+    const int64_t total = p.M_total * p.L;
+    const int64_t e0 = total * blockIdx.x / gridDim.x, e1 = total * (blockIdx.x + 1) / gridDim.x;
+    const uint64_t* lines = p.peer_stage[p.rank] + kLineWord / 2;
+    bool late = false;
+    for (int64_t e = e0 + threadIdx.x; e < e1; e += C::CW * 32) {
+      uint64_t v = 0;
+      uint64_t t0 = 0;
+      for (uint32_t it = 0;; ++it) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(lines + e) : "memory");
+        if ((uint32_t)(v >> 32) == epoch) break;
+        if (late) break;   // this thread already gave up once: do not wait again
+        if ((it & 63u) == 0) {
+          const uint64_t t = globaltimer();
+          if (it == 0) t0 = t;
+          else if (t - t0 > p.peer_wait_ns) {
+            atomicOr(p.err, kDevErrTimeoutPeer);
+            late = true;
+            break;
           }
         }
+      }
+      if ((uint32_t)(v >> 32) == epoch) {
+        const int64_t l = e / p.M_total, m = e % p.M_total;
+        p.c[l * p.c_sl + m * p.c_sm] = __ushort_as_half((unsigned short)(v & 0xFFFFu));
+      }
+    }
+    asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
+    if (threadIdx.x == 0) {
+      const uint32_t done = atomicAdd(ctl + kCtaCounter, 1u) + 1u;
+      if (done == gridDim.x) {
+        ctl[kCtaCounter] = 0u;
         const uint64_t te = globaltimer();
-        mine[kStampWord + 4] = (uint32_t)te;
-        mine[kStampWord + 5] = (uint32_t)(te >> 32);
-        if (p.epoch == 0) mine[kEpochWord] = epoch;
-        __threadfence_system();
+        ctl[kStampWord + 4] = (uint32_t)te;
+        ctl[kStampWord + 5] = (uint32_t)(te >> 32);
+        if (p.epoch == 0) ctl[kEpochWord] = epoch;
       }
     }
   }
@@ -612,16 +616,20 @@ extern "C" int nvfp4_set_peer_wait_ns(uint64_t ns) {
 extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sfa, const void* sfb,
                                     int64_t M_local, int64_t K, int64_t L, int64_t a_sm, int64_t a_sl,
                                     int64_t b_sl, int64_t sfa_sm, int64_t sfa_sl, int64_t sfb_sl,
-                                    void* const* peer_out, int64_t c_sm, int64_t c_sl, int64_t m_off,
-                                    uint32_t* const* peer_flags, int world, int rank, uint32_t epoch,
-                                    void* stream) {
+                                    void* out, int64_t c_sm, int64_t c_sl, int64_t m_off, int64_t M_total,
+                                    void* const* peer_stage, int world, int rank, uint32_t epoch, void* stream) {
   using namespace nvfp4;
-  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_out || !peer_flags)
-    return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: need 1 <= world <= %d and 0 <= rank < world", kMaxRanks);
-  for (int r = 0; r < world; ++r)
-    if (!peer_out[r] || !peer_flags[r]) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: null peer pointer");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world || !peer_stage || !out)
+    return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: need 1 <= world <= %d, 0 <= rank < world and an output",
+                kMaxRanks);
+  for (int r = 0; r < world; ++r) {
+    if (!peer_stage[r]) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: null staging buffer");
+    if (reinterpret_cast<uintptr_t>(peer_stage[r]) & 7u)
+      return fail(NVFP4_ERR_ALIGNMENT, "nvfp4_gemv_allgather: staging buffers must be 8-byte aligned");
+  }
   if (!a || !b || !sfa || !sfb) return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: null input");
-  if (M_local < 1 || L < 1 || K < 16 || K % 16 || m_off < 0 || c_sm == 0 || (L > 1 && c_sl == 0))
+  if (M_local < 1 || L < 1 || K < 16 || K % 16 || m_off < 0 || M_total < m_off + M_local || c_sm == 0 ||
+      (L > 1 && c_sl == 0))
     return fail(NVFP4_ERR_INVALID, "nvfp4_gemv_allgather: bad shape or strides");
   const bool tma_ok = aligned16(a) && aligned16(b) && aligned16(sfa) && aligned16(sfb) && a_sm % 16 == 0 &&
                       sfa_sm % 16 == 0 &&
@@ -632,24 +640,19 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
   args.b = static_cast<const uint8_t*>(b);
   args.sfa = static_cast<const uint8_t*>(sfa);
   args.sfb = static_cast<const uint8_t*>(sfb);
-  args.c = static_cast<__half*>(peer_out[rank]);
+  args.c = static_cast<__half*>(out);
   args.M = M_local; args.K = K; args.L = L;
   args.a_sm = a_sm; args.a_sl = a_sl; args.b_sl = b_sl;
   args.sfa_sm = sfa_sm; args.sfa_sl = sfa_sl; args.sfb_sl = sfb_sl;
   args.c_sm = c_sm; args.c_sl = c_sl;
   args.err = device_error_word();
   if (!args.err) return fail(NVFP4_ERR_CUDA, "nvfp4_gemv_allgather: cannot resolve the device error word");
-  for (int r = 0; r < world; ++r) {
-    args.peer_c[r] = static_cast<__half*>(peer_out[r]);
-    args.peer_flag[r] = peer_flags[r];
-  }
+  for (int r = 0; r < world; ++r) args.peer_stage[r] = static_cast<uint64_t*>(peer_stage[r]);
   args.world = world;
   args.rank = rank;
   args.m_off = m_off;
+  args.M_total = M_total;
   args.epoch = epoch;
-  bool vec = c_sm == 1 && m_off % 8 == 0 && (L == 1 || c_sl % 8 == 0);
-  for (int r = 0; r < world; ++r) vec = vec && aligned16(peer_out[r]);
-  args.vec_rows = vec ? 1 : 0;
   args.peer_wait_ns = g_peer_wait_ns.load(std::memory_order_relaxed);
   return gemv_dispatch(args, static_cast<cudaStream_t>(stream));
 }

@@ -135,14 +135,15 @@ class ShardedGroupedGemm:
 class FusedShardedGemv:
     """Row-sharded GEMV whose output all-gather is fused into the kernel.
 
-    Every rank owns a full-size output buffer [M, 1, L] (stored L-major, rows
-    contiguous) and a counter word, both in torch symmetric memory so every
-    GPU holds device pointers to every rank's copy.  One launch per call per
-    rank computes this rank's rows and stores them straight into all ranks'
-    buffers over NVLink (``nvfp4_gemv_allgather``); the launch returns once all
-    ranks' rows have landed locally.  No NCCL call on the data path.  The flag
-    words (per-source-rank epochs and a CTA counter) are reused across calls
-    with a running epoch, so one instance serves one fixed shape.
+    Every rank owns a staging buffer in torch symmetric memory (so every GPU
+    holds device pointers to every rank's copy) and a full-size local output
+    [M, 1, L].  One launch per call per rank computes this rank's rows and
+    sends every result, as one self-validating 64-bit line (epoch, fp16), to
+    every rank's staging buffer over NVLink (``nvfp4_gemv_allgather``); each
+    CTA then copies its slice of the lines into the output once they carry this
+    call's epoch, so the launch returns with all ranks' rows present.  No NCCL
+    call and no fence on the data path.  The staging buffers are reused across
+    calls with a running epoch, so one instance serves one fixed shape.
     """
 
     def __init__(self, M: int, K: int, L: int, group=None, device=None, device_epoch: bool = False):
@@ -151,7 +152,6 @@ class FusedShardedGemv:
         import ctypes
         import torch.distributed._symmetric_memory as symm
         self.device_epoch = device_epoch
-        from . import _lib
         self.M, self.K, self.L = M, K, L
         self.group = group or dist.group.WORLD
         self.world = dist.get_world_size(self.group)
@@ -160,21 +160,25 @@ class FusedShardedGemv:
             raise ValueError("FusedShardedGemv supports up to 8 ranks")
         self.lo, self.hi = row_split(M, self.world, self.rank)
         dev = device or torch.device("cuda", torch.cuda.current_device())
-        self.out_flat = symm.empty(L * M, dtype=torch.float16, device=dev)
-        self.flags = symm.empty(64, dtype=torch.int32, device=dev)
-        self.flags.zero_()
+        self.out_flat = torch.empty(L * M, dtype=torch.float16, device=dev)
+        # 64 control words, then one 64-bit line per output element
+        self.stage = symm.empty(64 + 2 * M * L, dtype=torch.int32, device=dev)
+        self.stage.zero_()
         torch.cuda.synchronize(dev)
-        gname = self.group.group_name
-        self._h_out = symm.rendezvous(self.out_flat, gname)
-        self._h_flag = symm.rendezvous(self.flags, gname)
-        self._peer_out = (ctypes.c_void_p * self.world)(*self._h_out.buffer_ptrs)
-        self._peer_flag = (ctypes.c_void_p * self.world)(*self._h_flag.buffer_ptrs)
+        self._h_stage = symm.rendezvous(self.stage, self.group.group_name)
+        self._peer_stage = (ctypes.c_void_p * self.world)(*self._h_stage.buffer_ptrs)
         self.epoch = 0
         dist.barrier(self.group)
 
     def out(self) -> torch.Tensor:
         """[M, 1, L] view of this rank's copy of the full output."""
         return self.out_flat.view(self.L, 1, self.M).permute(2, 1, 0)
+
+    def stamps(self) -> tuple[int, int, int]:
+        """%globaltimer (ns) of the last call on this rank: launch start, CTA 0
+        having sent its rows, last CTA holding its slice of the output."""
+        w = self.stage[32:38].cpu().numpy().view("uint32").astype("uint64")
+        return tuple(int(w[2 * i]) | (int(w[2 * i + 1]) << 32) for i in range(3))
 
     def __call__(self, a_rows, b, sfa_rows, sfb) -> torch.Tensor:
         from . import _lib
@@ -183,6 +187,6 @@ class FusedShardedGemv:
         _lib.check(_lib.lib().nvfp4_gemv_allgather(
             a_rows.data_ptr(), b.data_ptr(), sfa_rows.data_ptr(), sfb.data_ptr(),
             self.hi - self.lo, self.K, self.L, sa[0], sa[2], sb[2], ssa[0], ssa[2], ssb[2],
-            self._peer_out, 1, self.M, self.lo, self._peer_flag, self.world, self.rank, self.epoch,
-            torch.cuda.current_stream().cuda_stream))
+            self.out_flat.data_ptr(), 1, self.M, self.lo, self.M, self._peer_stage, self.world, self.rank,
+            self.epoch, torch.cuda.current_stream().cuda_stream))
         return self.out()

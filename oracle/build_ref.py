@@ -18,7 +18,9 @@ The built module is used in two places only:
   as committed fixtures so the CPU-only tests can pin the oracle too.
 
 Nothing here reads the reference at run time on the GPU box: the ``.so`` is
-built in the development container, where the source exists.
+built in the development container, where the source exists.  The source file
+is named by ``--src PATH`` or the ``NVFP4_REF_SRC`` environment variable; with
+neither, an already built module is kept and nothing is compiled.
 """
 from __future__ import annotations
 
@@ -29,7 +31,7 @@ import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
-REF_SRC = os.environ.get("NVFP4_REF_SRC", "/root/reference/blackwell_nvfp4_gemv.cu")
+REF_SRC = os.environ.get("NVFP4_REF_SRC")
 MODULE = "ref_nvfp4_gemv"
 SO_PATH = os.path.join(OUT_DIR, MODULE + sysconfig.get_config_var("EXT_SUFFIX"))
 
@@ -42,13 +44,15 @@ def _torch_paths():
     return inc, os.path.join(tdir, "lib"), torch.compiled_with_cxx11_abi()
 
 
-def build(force: bool = False, verbose: bool = False) -> str | None:
-    """Compile the reference into ``oracle/_ref``.  Returns the .so path, or
-    None when the reference source is absent (as on the GPU box)."""
-    if not os.path.exists(REF_SRC):
+def build(force: bool = False, verbose: bool = False, src: str | None = None) -> str | None:
+    """Compile the reference source ``src`` (default: ``NVFP4_REF_SRC``) into
+    ``oracle/_ref``.  Returns the .so path, or None when no source is named or
+    it is absent (as on the GPU box) and nothing was built before."""
+    src = src or REF_SRC
+    if not src or not os.path.exists(src):
         return SO_PATH if os.path.exists(SO_PATH) else None
     if (not force and os.path.exists(SO_PATH)
-            and os.path.getmtime(SO_PATH) >= os.path.getmtime(REF_SRC)
+            and os.path.getmtime(SO_PATH) >= os.path.getmtime(src)
             and os.path.getmtime(SO_PATH) >= os.path.getmtime(__file__)):
         return SO_PATH
     os.makedirs(OUT_DIR, exist_ok=True)
@@ -59,7 +63,7 @@ def build(force: bool = False, verbose: bool = False) -> str | None:
             f"-D_GLIBCXX_USE_CXX11_ABI={int(cxx11)}"]
     nvcc = ["nvcc", "-std=c++17", "-O3", "-gencode", "arch=compute_100a,code=sm_100a",
             "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", *defs,
-            *[f"-I{p}" for p in inc], f"-I{py_inc}", "-c", REF_SRC, "-o", obj]
+            *[f"-I{p}" for p in inc], f"-I{py_inc}", "-c", src, "-o", obj]
     link = ["g++", "-shared", "-o", SO_PATH, obj, f"-L{libdir}", "-lc10", "-lc10_cuda",
             "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
             "-L/usr/local/cuda/lib64", "-lcudart", f"-Wl,-rpath,{libdir}"]
@@ -86,5 +90,7 @@ def load():
 
 
 if __name__ == "__main__":
-    p = build(force="--force" in sys.argv, verbose=True)
+    args = sys.argv[1:]
+    src = args[args.index("--src") + 1] if "--src" in args else None
+    p = build(force="--force" in args, verbose=True, src=src)
     print(p)

@@ -79,17 +79,22 @@ def test_gemm_entry_points_reject_bad_arguments_without_gpu(pkg):
 
 def test_allgather_rejects_bad_world_without_gpu(pkg):
     l = pkg._lib.lib()
-    outs = (ctypes.c_void_p * 8)(*([4096] * 8))
-    flags = (ctypes.c_void_p * 8)(*([4096] * 8))
+    stages = (ctypes.c_void_p * 8)(*([4096] * 8))
+    # a, b, sfa, sfb, M_local, K, L, strides (6), out, c_sm, c_sl, m_off, M_total, stages, world, rank, epoch, stream
     args = lambda world, rank: (4096, 4096, 4096, 4096, 64, 512, 1, 256, 0, 0, 32, 0, 0,
-                                ctypes.cast(outs, ctypes.c_void_p), 1, 0, 0, ctypes.cast(flags, ctypes.c_void_p),
-                                world, rank, 1, None)
+                                4096, 1, 0, 0, 128, stages, world, rank, 1, None)
     assert l.nvfp4_gemv_allgather(*args(9, 0)) == 1 and b"world" in l.nvfp4_last_error()
     assert l.nvfp4_gemv_allgather(*args(2, 2)) == 1
     nulls = (ctypes.c_void_p * 8)()
     a = list(args(2, 0))
-    a[13] = ctypes.cast(nulls, ctypes.c_void_p)
-    assert l.nvfp4_gemv_allgather(*a) == 1 and b"null peer" in l.nvfp4_last_error()
+    a[18] = nulls
+    assert l.nvfp4_gemv_allgather(*a) == 1 and b"null staging" in l.nvfp4_last_error()
+    odd = (ctypes.c_void_p * 8)(*([4100] * 8))
+    a[18] = odd
+    assert l.nvfp4_gemv_allgather(*a) == 2 and b"8-byte" in l.nvfp4_last_error()
+    a = list(args(2, 0))
+    a[17] = 32                                  # M_total below m_off + M_local
+    assert l.nvfp4_gemv_allgather(*a) == 1 and b"shape" in l.nvfp4_last_error()
 
 
 def test_gemv_forward_checks_sizes_against_tensors(pkg):

