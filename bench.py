@@ -410,13 +410,14 @@ def gather_rows(world, values):
     return [o.tolist() for o in out]
 
 
-def gather_stamps(fused, step, world, n=20):
+def gather_stamps(fused, step, world, align, n=20):
     """Per-rank medians over n synchronised calls of the fused gather's
     %globaltimer stamps: CTA 0's rows sent and all ranks' rows present, in us
     after the rank's launch began, plus each rank's start relative to the
     earliest (GPU timers of one node; offsets between them are not removed)."""
     pub, seen, starts = [], [], []
     for _ in range(n):
+        align()
         step([])
         torch.cuda.synchronize()
         t0, t1, t2 = fused.stamps()
@@ -512,7 +513,8 @@ def headline_config(world):
             (f", row-sharded x{world}, all-gather fused into the kernel (NVLink peer stores)" if world > 1 else ""),
             "M": HEADLINE["M"], "K": HEADLINE["K"], "L": HEADLINE["L"],
             "l2": "flushed before every step (512 MiB write, then 256 MiB read)" +
-            ("; ranks aligned by a 1-element all-reduce before each step, outside the timed events"
+            ("; ranks aligned by a device-side barrier over symmetric memory before each step, "
+             "outside the timed events"
              if world > 1 else ""),
             "parallelism": f"rows/{world}" if world > 1 else "single GPU"}
 
@@ -533,9 +535,11 @@ def our_arm(args, world, rank, local):
     fused = pkg.sharded.FusedShardedGemv(M, K, L) if world > 1 else None
     align = None
     if world > 1:
-        import torch.distributed as dist
-        one = torch.zeros(1, device=dev)
-        align = lambda: dist.all_reduce(one)
+        # line the ranks up before each step (outside the timed events) with a
+        # device-side barrier over the fused gather's symmetric buffers: ranks
+        # leave it within a peer round trip; a 1-element NCCL all-reduce spreads
+        # its completion over several microseconds at 8 ranks
+        align = fused.barrier
 
     def step_split(ev):
         # one GEMV; with world > 1 the fused kernel also delivers every rank's rows
@@ -599,7 +603,7 @@ def our_arm(args, world, rank, local):
         nccl_step, nccl_kern = max_over_ranks(world, [statistics.mean(sum(s) for s in nsegs),
                                                       statistics.mean(s[0] for s in nsegs)])
         mean_kern = nccl_kern
-        stamps = gather_stamps(fused, step_split, world)
+        stamps = gather_stamps(fused, step_split, world, align)
         grouped_ok, grouped_line = run_grouped_sharded_extra(pkg, flush, max(10, args.steps // 2), args.warmup,
                                                              world, align, fp4_peak_tflops(pkg))
         if not all_ok(world, grouped_ok):

@@ -174,6 +174,14 @@ class FusedShardedGemv:
         """[M, 1, L] view of this rank's copy of the full output."""
         return self.out_flat.view(self.L, 1, self.M).permute(2, 1, 0)
 
+    def barrier(self, timeout_ms: int = 10000) -> None:
+        """Device-side barrier over this instance's staging buffers (each rank
+        signals every peer over NVLink and waits for all), enqueued on the
+        current stream: ranks leave it within a peer round trip of each other,
+        which lines their next launches up far tighter than a collective does.
+        Bounded by timeout_ms."""
+        self._h_stage.barrier(channel=0, timeout_ms=timeout_ms)
+
     def stamps(self) -> tuple[int, int, int]:
         """%globaltimer (ns) of the last call on this rank: launch start, CTA 0
         having sent its rows, last CTA holding its slice of the output."""
