@@ -410,13 +410,14 @@ def gather_rows(world, values):
     return [o.tolist() for o in out]
 
 
-def gather_stamps(fused, step, world, align, n=20):
+def gather_stamps(fused, step, world, align, flush, n=20):
     """Per-rank medians over n synchronised calls of the fused gather's
     %globaltimer stamps: CTA 0's rows sent and all ranks' rows present, in us
     after the rank's launch began, plus each rank's start relative to the
     earliest (GPU timers of one node; offsets between them are not removed)."""
     pub, seen, starts = [], [], []
     for _ in range(n):
+        flush()      # GPU work ahead of the barrier, so every rank has enqueued its launch when it opens
         align()
         step([])
         torch.cuda.synchronize()
@@ -603,7 +604,7 @@ def our_arm(args, world, rank, local):
         nccl_step, nccl_kern = max_over_ranks(world, [statistics.mean(sum(s) for s in nsegs),
                                                       statistics.mean(s[0] for s in nsegs)])
         mean_kern = nccl_kern
-        stamps = gather_stamps(fused, step_split, world, align)
+        stamps = gather_stamps(fused, step_split, world, align, flush)
         grouped_ok, grouped_line = run_grouped_sharded_extra(pkg, flush, max(10, args.steps // 2), args.warmup,
                                                              world, align, fp4_peak_tflops(pkg))
         if not all_ok(world, grouped_ok):

@@ -86,10 +86,13 @@ NVFP4_API int nvfp4_gemv_grid(int64_t M, int64_t K, int64_t L, int64_t* grid);
  * peer_stage[r] is rank r's staging buffer, a device pointer valid on this GPU
  * (peer memory over NVLink, e.g. from torch symmetric memory), 8-byte aligned,
  * zero-initialised, of at least 64 + 2 * M_total * L 32-bit words.  Protocol:
- * element (m, l) travels as one 64-bit line (epoch << 32 | fp16 bits) to index
- * 32 + l * M_total + m (in 64-bit units) of every rank's buffer; a naturally
+ * results travel as 64-bit lines (epoch << 32 | fp16 bits) to every rank's
+ * buffer, from 64-bit index 32 on.  When M_total is even a line holds two
+ * elements, e = 2i and 2i + 1 (e = l * M_total + m) in line i, low half first,
+ * and every rank's m_off and M_local must then be even (NVFP4_ERR_INVALID
+ * otherwise); when M_total is odd a line holds element e = i.  A naturally
  * aligned 64-bit store is single-copy atomic, so a line carrying this call's
- * epoch carries this call's value and no fence or counter gates it.  Each CTA
+ * epoch carries this call's values and no fence or counter gates it.  Each CTA
  * then copies its slice of the lines into `out`, waiting for each to carry the
  * epoch.  Words 0-63 of this rank's buffer are control words: 16 counts
  * finished CTAs (reset by the last one), 20 holds the epoch in device-epoch

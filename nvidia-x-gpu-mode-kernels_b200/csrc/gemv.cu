@@ -45,11 +45,13 @@ namespace {
 
 constexpr int kMaxRanks = 8;
 // Staging buffer of the fused all-gather (32-bit words): control words first,
-// then one 64-bit line per output element from word kLineWord on.
+// then 64-bit lines from word kLineWord on: (epoch << 32) | two fp16 values
+// (elements 2i, 2i+1 in line i) when M_total is even, (epoch << 32) | one
+// fp16 value (element i in line i) when it is odd.
 constexpr int kCtaCounter = 16;   // counts this rank's finished CTAs (reset per call)
 constexpr int kEpochWord = 20;    // the last epoch (device-epoch mode)
 constexpr int kStampWord = 32;    // words 32-37: %globaltimer at start / rows sent / all rows present
-constexpr int kLineWord = 64;     // first line: element e at 64-bit index kLineWord / 2 + e
+constexpr int kLineWord = 64;     // first line: 64-bit index kLineWord / 2
 
 
 struct GemvArgs {
@@ -71,6 +73,7 @@ struct GemvArgs {
   int rank;
   int64_t m_off;
   int64_t M_total;
+  int per_line;      // output elements per 64-bit line: 2 (M_total even) or 1
   uint32_t epoch;    // 1-based call count of this gather (same on every rank); 0 = device epoch
   uint64_t peer_wait_ns;   // budget of the wait for the other ranks' rows
 };
@@ -280,18 +283,25 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
         if (m0 + row < M) p.c[l * p.c_sl + (m0 + row) * p.c_sm] = __float2half_rn(v);
       }
     } else {
-      // one 64-bit line per (row, rank): thread t sends row t % ROWS to rank
-      // t / ROWS.  A naturally aligned 64-bit store is single-copy atomic, so a
-      // line that carries this call's epoch carries this call's value: no
-      // fence or count is needed before the receiver may use it.
-      for (int t = threadIdx.x; t < C::ROWS * p.world; t += C::CW * 32) {
-        const int row = t % C::ROWS, r = t / C::ROWS;
+      // one 64-bit line per (row group, rank), a row group being per_line
+      // consecutive rows (rows are split at even boundaries when per_line is
+      // 2, so a pair never straddles two ranks): thread t sends group t % G to
+      // rank t / G.  A naturally aligned 64-bit store is single-copy atomic, so
+      // a line that carries this call's epoch carries this call's values: no
+      // fence or count is needed before the receiver may use it.  Two values
+      // per line halve the small NVLink stores, whose rate limits the gather.
+      const int pl = p.per_line, G = C::ROWS / pl;
+      for (int t = threadIdx.x; t < G * p.world; t += C::CW * 32) {
+        const int row = (t % G) * pl, r = t / G;
         if (m0 + row >= M) continue;
-        float v = 0.f;
+        uint64_t line = (uint64_t)epoch << 32;
+        for (int j = 0; j < pl; ++j) {
+          float v = 0.f;
 #pragma unroll
-        for (int c = 0; c < C::NCH; ++c) v += rb[row * C::NCH + c];
-        const uint64_t line = ((uint64_t)epoch << 32) | __half_as_ushort(__float2half_rn(v));
-        uint64_t* dst = p.peer_stage[r] + kLineWord / 2 + l * p.M_total + p.m_off + m0 + row;
+          for (int c = 0; c < C::NCH; ++c) v += rb[(row + j) * C::NCH + c];
+          line |= (uint64_t)__half_as_ushort(__float2half_rn(v)) << (16 * j);
+        }
+        uint64_t* dst = p.peer_stage[r] + kLineWord / 2 + (l * p.M_total + p.m_off + m0 + row) / pl;
         asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(dst), "l"(line) : "memory");   // NVLink peer store
       }
     }
@@ -308,7 +318,7 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
       ctl[kStampWord + 2] = (uint32_t)ts;
       ctl[kStampWord + 3] = (uint32_t)(ts >> 32);
     }
-    const int64_t total = p.M_total * p.L;
+    const int64_t total = p.M_total * p.L / p.per_line;   // lines
     const int64_t e0 = total * blockIdx.x / gridDim.x, e1 = total * (blockIdx.x + 1) / gridDim.x;
     const uint64_t* lines = p.peer_stage[p.rank] + kLineWord / 2;
     bool late = false;
@@ -330,8 +340,10 @@ gemv_tma_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ G
         }
       }
       if ((uint32_t)(v >> 32) == epoch) {
-        const int64_t l = e / p.M_total, m = e % p.M_total;
-        p.c[l * p.c_sl + m * p.c_sm] = __ushort_as_half((unsigned short)(v & 0xFFFFu));
+        for (int j = 0; j < p.per_line; ++j) {
+          const int64_t x = e * p.per_line + j, l = x / p.M_total, m = x % p.M_total;
+          p.c[l * p.c_sl + m * p.c_sm] = __ushort_as_half((unsigned short)((v >> (16 * j)) & 0xFFFFu));
+        }
       }
     }
     asm volatile("bar.sync 1, %0;" :: "r"(C::CW * 32) : "memory");
@@ -635,6 +647,10 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
                       sfa_sm % 16 == 0 &&
                       (L == 1 || (a_sl % 16 == 0 && b_sl % 16 == 0 && sfa_sl % 16 == 0 && sfb_sl % 16 == 0));
   if (!tma_ok) return fail(NVFP4_ERR_ALIGNMENT, "nvfp4_gemv_allgather: needs 16-byte aligned pointers and strides");
+  if (M_total % 2 == 0 && (m_off % 2 || M_local % 2))
+    return fail(NVFP4_ERR_INVALID,
+                "nvfp4_gemv_allgather: with an even M_total, every rank's m_off and M_local must be even "
+                "(two results travel per line)");
   GemvArgs args{};
   args.a = static_cast<const uint8_t*>(a);
   args.b = static_cast<const uint8_t*>(b);
@@ -652,6 +668,7 @@ extern "C" int nvfp4_gemv_allgather(const void* a, const void* b, const void* sf
   args.rank = rank;
   args.m_off = m_off;
   args.M_total = M_total;
+  args.per_line = M_total % 2 == 0 ? 2 : 1;
   args.epoch = epoch;
   args.peer_wait_ns = g_peer_wait_ns.load(std::memory_order_relaxed);
   return gemv_dispatch(args, static_cast<cudaStream_t>(stream));

@@ -158,7 +158,8 @@ class FusedShardedGemv:
         self.rank = dist.get_rank(self.group)
         if self.world > 8:
             raise ValueError("FusedShardedGemv supports up to 8 ranks")
-        self.lo, self.hi = row_split(M, self.world, self.rank)
+        # even boundaries: with an even M two results travel per 64-bit line
+        self.lo, self.hi = row_split(M, self.world, self.rank, align=2)
         dev = device or torch.device("cuda", torch.cuda.current_device())
         self.out_flat = torch.empty(L * M, dtype=torch.float16, device=dev)
         # 64 control words, then one 64-bit line per output element

@@ -33,7 +33,10 @@ def check_gemv(pkg, rank, world):
         torch.cuda.synchronize()
         assert torch.equal(sh.full(), ref), f"NCCL-gathered vs single-GPU mismatch at M={M} K={K} L={L}"
         fused = pkg.sharded.FusedShardedGemv(M, K, L)
-        for _ in range(3):                  # repeated calls reuse the flag words
+        # the fused gather splits rows at even boundaries (two results per line)
+        fsub = lambda t: t[fused.lo:fused.hi].permute(2, 0, 1).contiguous().permute(1, 2, 0)
+        a, sfa = fsub(full.a), fsub(full.sfa)
+        for _ in range(3):                  # repeated calls reuse the staging buffers
             out = fused(a, full.b, sfa, full.sfb)
         torch.cuda.synchronize()
         assert pkg._lib.device_errors() == 0, "device error word set"

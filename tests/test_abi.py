@@ -95,6 +95,9 @@ def test_allgather_rejects_bad_world_without_gpu(pkg):
     a = list(args(2, 0))
     a[17] = 32                                  # M_total below m_off + M_local
     assert l.nvfp4_gemv_allgather(*a) == 1 and b"shape" in l.nvfp4_last_error()
+    a = list(args(2, 0))
+    a[4] = 63                                   # odd share of an even M_total: two results per line
+    assert l.nvfp4_gemv_allgather(*a) == 1 and b"even" in l.nvfp4_last_error()
 
 
 def test_gemv_forward_checks_sizes_against_tensors(pkg):

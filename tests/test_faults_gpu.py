@@ -34,9 +34,12 @@ def _allgather(pkg, x, rows, out, stages, world, rank, epoch, m_off=0):
 
 
 def _lines(stage, M):
-    """The 64-bit lines of a staging buffer: (epoch, fp16 bits) per element."""
-    v = stage[64: 64 + 2 * M].cpu().numpy().view(np.uint64)
-    return (v >> np.uint64(32)).astype(np.uint32), (v & np.uint64(0xFFFF)).astype(np.uint16)
+    """The 64-bit lines of a staging buffer for an even M: (epoch per line,
+    fp16 bits per element; two elements per line, low half first)."""
+    v = stage[64: 64 + M].cpu().numpy().view(np.uint64)
+    ep = (v >> np.uint64(32)).astype(np.uint32)
+    bits = np.stack([(v & np.uint64(0xFFFF)), (v >> np.uint64(16)) & np.uint64(0xFFFF)], axis=1)
+    return ep, bits.astype(np.uint16).reshape(-1)
 
 
 def test_fused_gather_peer_wait_expires_and_recovers(pkg, oracle, cuda):
@@ -66,7 +69,7 @@ def test_fused_gather_peer_wait_expires_and_recovers(pkg, oracle, cuda):
         want_bits = want.cpu().numpy().view(np.uint16)
         for st in stages:                                    # rank 0 sent its lines to both ranks
             ep, bits = _lines(st, M)
-            assert (ep[:half] == 1).all() and (ep[half:] == 0).all()
+            assert (ep[: half // 2] == 1).all() and (ep[half // 2:] == 0).all()
             assert np.array_equal(bits[:half], want_bits[:half])
         ctl = stages[0].cpu()
         assert ctl[16] == 0                                  # CTA count reset for the next call
@@ -74,8 +77,9 @@ def test_fused_gather_peer_wait_expires_and_recovers(pkg, oracle, cuda):
         t_start, t_sent, t_end = (int(w[2 * i]) | (int(w[2 * i + 1]) << 32) for i in range(3))
         assert t_start <= t_sent <= t_end and t_end - t_start >= 1_000_000
         # rank 1 "delivers" its rows of call 2: the same buffers complete it without error
-        lines = (np.uint64(2) << np.uint64(32)) | want_bits[half:].astype(np.uint64)
-        stages[0][64 + 2 * half: 64 + 2 * M] = torch.from_numpy(lines.view(np.int32)).to(cuda)
+        pairs = want_bits[half:].astype(np.uint64).reshape(-1, 2)
+        lines = (np.uint64(2) << np.uint64(32)) | pairs[:, 0] | (pairs[:, 1] << np.uint64(16))
+        stages[0][64 + half: 64 + M] = torch.from_numpy(lines.view(np.int32)).to(cuda)
         out.fill_(float("nan"))
         pkg._lib.check(_allgather(pkg, xr, half, out, stages, 2, 0, epoch=2))
         torch.cuda.synchronize()
@@ -95,7 +99,7 @@ def test_fused_gather_peer_wait_expires_and_recovers(pkg, oracle, cuda):
 def test_fused_gather_world1_matches_plain_kernel(pkg, cuda):
     """A 1-rank fused launch (staging buffer local) returns exactly the plain
     kernel's output, call after call, and in device-epoch mode too."""
-    for M, K, L in ((16384, 16384, 1), (1000, 2048, 3)):
+    for M, K, L in ((16384, 16384, 1), (1000, 2048, 3), (999, 2048, 2)):   # two / one result(s) per line
         x = pkg.inputs.gemv_inputs(M, K, L, seed=2, device=cuda)
         pkg.custom_kernel(*x.as_tuple())
         torch.cuda.synchronize()
